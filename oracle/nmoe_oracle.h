@@ -1,0 +1,122 @@
+/*
+ * nmoe_oracle.h -- CPU restatement of nmoe's routed-MoE block (TEST INFRASTRUCTURE).
+ *
+ * This library is the checker for the CUDA path, never part of the product:
+ * only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / reference
+ * arm may load it.  Every function cites the reference file:line it restates
+ * (paths are relative to the nano-metal-moe-qwen36 project root).
+ *
+ * Parity pins: the quantiser is checked bit-exactly against fixtures produced by
+ * importing the reference's scripts/convert_qwen36.py (tests/golden/make_golden.py);
+ * the routing math (softmax / top-k / renormalise / SwiGLU / dequant matvec) is
+ * checked bit-exactly against the reference's own src/math.m compiled as C into
+ * oracle/_ref/ (oracle/Makefile, target `ref`).  The Metal kernels themselves
+ * cannot run here (no Apple GPU); their fp32 math is restated below.
+ */
+#ifndef NMOE_ORACLE_H
+#define NMOE_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ORC_HIDDEN 2048
+#define ORC_INTER 512
+#define ORC_EXPERTS 256
+#define ORC_GROUP 64
+#define ORC_MAX_K 8
+
+enum { ORC_DTYPE_BF16 = 1, ORC_DTYPE_Q4 = 4, ORC_DTYPE_Q2 = 2, ORC_DTYPE_F32 = 0 };
+
+/* bf16 <-> f32 (src/math.m:7-19, scripts/convert_qwen36.py:147-155) */
+float orc_bf16_to_f32(uint16_t v);
+uint16_t orc_f32_to_bf16(float v);
+void orc_f32_to_bf16_array(const float *in, uint16_t *out, size_t n);
+void orc_bf16_to_f32_array(const uint16_t *in, float *out, size_t n);
+
+/* Affine group-64 quantiser (scripts/convert_qwen36.py:158-211).
+ * packed: rows x (in_dim*bits/32) u32, scales/biases: rows x (in_dim/64) bf16. */
+int orc_quantize_rows(const uint16_t *rows_bf16, size_t rows, size_t in_dim, int bits,
+                      uint32_t *packed, uint16_t *scales, uint16_t *biases);
+
+/* Expert blob layout (scripts/convert_qwen36.py:38-64; src/runtime.m:2240-2252). */
+size_t orc_expert_size(int bits);
+int orc_expert_offsets(int bits, size_t off[9]);
+/* gate_up_bf16: [1024][2048] (rows 0-511 gate, 512-1023 up), down_bf16: [2048][512]
+ * (scripts/convert_qwen36.py:377-409). */
+int orc_pack_expert(const uint16_t *gate_up_bf16, const uint16_t *down_bf16, int bits, uint8_t *blob);
+
+/* src/math.m restatements */
+float orc_sigmoid_cpu(float x);                                            /* math.m:21-28 */
+float orc_sigmoid_kernel(float x);                                         /* kernels.metal:177-179 */
+void orc_softmax(float *values, size_t count);                             /* math.m:67-93 */
+size_t orc_topk(const float *values, size_t count, size_t k, uint32_t *indices,
+                float *selected);                                          /* math.m:95-132 */
+void orc_renormalize(float *values, size_t count);                         /* math.m:134-153 */
+void orc_swiglu(const float *gate, const float *up, float *out, size_t n); /* kernels.metal:1352-1361 */
+/* math.m:236-274: sequential fp32 accumulation, (q*scale + bias) * x. */
+void orc_dequant_matvec_seq(const uint32_t *packed, const uint16_t *scales, const uint16_t *biases,
+                            const float *x, float *y, size_t rows, size_t in_dim, int bits);
+
+/* Kernel-form matvecs: 32 lane-strided fp32 partial sums (one per SIMD lane, as the
+ * Metal kernels stride packed words by lane) reduced by a butterfly tree.
+ * form 0: acc += fma(q, s, b) * x      (kernels.metal:192-238, 562-640, 642-714, 1456-1542)
+ * form 1: acc += fma(q, s*x, b*x)      (kernels.metal:240-301, 384-514)                */
+void orc_dequant_matvec(const uint32_t *packed, const uint16_t *scales, const uint16_t *biases,
+                        const float *x, float *y, size_t rows, size_t in_dim, int bits, int form);
+/* bf16 weights (no reference kernel): same lane-strided fp32 structure. */
+void orc_bf16_matvec(const uint16_t *w, const float *x, float *y, size_t rows, size_t in_dim);
+
+/* A dense (non-expert) matrix: bf16 [rows][cols] or q4 (weight u32, scales, biases). */
+typedef struct orc_dense {
+    int dtype;                 /* ORC_DTYPE_BF16 or ORC_DTYPE_Q4 */
+    const void *weight;
+    const uint16_t *scales;    /* q4 only */
+    const uint16_t *biases;    /* q4 only */
+} orc_dense;
+
+typedef struct orc_layer {
+    int bits;                  /* expert quantisation: 4 or 2 */
+    const uint8_t *experts;    /* layer_XX.bin image: num_experts * expert_size bytes */
+    size_t num_experts;
+    orc_dense router;          /* [256][2048]  (model.layers.N.mlp.gate) */
+    orc_dense shared_gate;     /* [512][2048]  (mlp.shared_expert.gate_proj) */
+    orc_dense shared_up;       /* [512][2048]  (mlp.shared_expert.up_proj) */
+    orc_dense shared_down;     /* [2048][512]  (mlp.shared_expert.down_proj) */
+    orc_dense shared_gate_vec; /* [1][2048]    (mlp.shared_expert_gate) */
+} orc_layer;
+
+/* Per-expert products (kernels.metal:562-640 q4 / 192-238+1352-1361 q2, 642-714). */
+void orc_expert_gate_up(const uint8_t *blob, int bits, const float *x, float *act);
+void orc_expert_down(const uint8_t *blob, int bits, const float *act, float *out);
+
+/* Router + shared gate/up + shared score (kernels.metal:384-514 for q4; bf16 analog). */
+void orc_route_shared(const orc_layer *L, const float *x, float *logits, float *shared_act, float *score);
+
+/* One routed-MoE block for one token, following the default q4 path
+ * (src/runtime.m:3151-3166 -> 1498-1511 -> 2778-2903, 2976-2983) and the q2 path
+ * (src/runtime.m:2841-2888).
+ *   k: active experts 1..8 (src/runtime.m:2923 clamp; here out-of-range -> -1)
+ *   x: fp32[2048]; h_mid: fp32[2048] or NULL (treated as zero)
+ *   logits_override: if non-NULL, route on these 256 logits instead of the computed ones
+ * Outputs (each may be NULL): out[2048], idx[8], w[8] (zero padded), logits[256],
+ * shared_act[512], score[1]. Returns 0 on success. */
+int orc_moe_block_forward(const orc_layer *L, int k, const float *x, const float *h_mid,
+                          const float *logits_override, float *out, uint32_t *idx, float *w,
+                          float *logits, float *shared_act, float *score);
+
+/* Batched block: T tokens, each routed independently (same math as above per token). */
+int orc_moe_block_forward_batched(const orc_layer *L, int T, int k, const float *x,
+                                  const float *h_mid, float *out, uint32_t *idx, float *w);
+
+/* Set the OpenMP thread count used by the matvecs (0 = library default). */
+void orc_set_threads(int n);
+int orc_get_threads(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

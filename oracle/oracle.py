@@ -1,0 +1,278 @@
+"""ctypes bindings for the CPU oracle (oracle/libnmoe_oracle.so) -- TEST INFRASTRUCTURE.
+
+Only tests/, __graft_entry__.smoke() and bench.py (cpu_baseline and the reference
+arm) may import this module; the product path never does.  It also wraps the
+reference's own src/math.m compiled unchanged into oracle/_ref/ when that library
+exists (built in the development container by `make -C oracle ref`).
+
+Also holds the seeded synthetic-weight generators shared by tests and bench.py:
+weights are drawn bf16 ~N(0, 0.02) and quantised by the restated
+scripts/convert_qwen36.py quantiser (orc_quantize_rows).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+from dataclasses import dataclass, field
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libnmoe_oracle.so")
+REF_LIB_PATH = os.path.join(HERE, "_ref", "libnmoe_math_ref.so")
+
+HIDDEN, INTER, EXPERTS, GROUP, MAX_K = 2048, 512, 256, 64, 8
+DTYPE_BF16, DTYPE_Q4, DTYPE_Q2 = 1, 4, 2
+
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+_u16p = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
+_u32p = np.ctypeslib.ndpointer(np.uint32, flags="C_CONTIGUOUS")
+_u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
+
+
+def build(quiet: bool = True) -> None:
+    """Compile the oracle (and the reference math.m when the reference tree exists)."""
+    out = subprocess.DEVNULL if quiet else None
+    subprocess.run(["make", "-C", HERE, "all"], check=True, stdout=out)
+    ref_root = os.environ.get("NMOE_REF_ROOT", "/root/reference")
+    if os.path.isfile(os.path.join(ref_root, "src", "math.m")):
+        subprocess.run(["make", "-C", HERE, "ref", f"REF_ROOT={ref_root}"], check=True, stdout=out)
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = C.CDLL(LIB_PATH)
+        L.orc_bf16_to_f32.restype = C.c_float
+        L.orc_bf16_to_f32.argtypes = [C.c_uint16]
+        L.orc_f32_to_bf16.restype = C.c_uint16
+        L.orc_f32_to_bf16.argtypes = [C.c_float]
+        L.orc_f32_to_bf16_array.argtypes = [_f32p, _u16p, C.c_size_t]
+        L.orc_quantize_rows.restype = C.c_int
+        L.orc_quantize_rows.argtypes = [_u16p, C.c_size_t, C.c_size_t, C.c_int, _u32p, _u16p, _u16p]
+        L.orc_expert_size.restype = C.c_size_t
+        L.orc_expert_size.argtypes = [C.c_int]
+        L.orc_expert_offsets.restype = C.c_int
+        L.orc_expert_offsets.argtypes = [C.c_int, C.POINTER(C.c_size_t)]
+        L.orc_pack_expert.restype = C.c_int
+        L.orc_pack_expert.argtypes = [_u16p, _u16p, C.c_int, _u8p]
+        L.orc_sigmoid_cpu.restype = C.c_float
+        L.orc_sigmoid_cpu.argtypes = [C.c_float]
+        L.orc_sigmoid_kernel.restype = C.c_float
+        L.orc_sigmoid_kernel.argtypes = [C.c_float]
+        L.orc_softmax.argtypes = [_f32p, C.c_size_t]
+        L.orc_topk.restype = C.c_size_t
+        L.orc_topk.argtypes = [_f32p, C.c_size_t, C.c_size_t, _u32p, _f32p]
+        L.orc_renormalize.argtypes = [_f32p, C.c_size_t]
+        L.orc_swiglu.argtypes = [_f32p, _f32p, _f32p, C.c_size_t]
+        L.orc_dequant_matvec_seq.argtypes = [_u32p, _u16p, _u16p, _f32p, _f32p, C.c_size_t, C.c_size_t, C.c_int]
+        L.orc_dequant_matvec.argtypes = [_u32p, _u16p, _u16p, _f32p, _f32p, C.c_size_t, C.c_size_t, C.c_int, C.c_int]
+        L.orc_bf16_matvec.argtypes = [_u16p, _f32p, _f32p, C.c_size_t, C.c_size_t]
+        L.orc_expert_gate_up.argtypes = [_u8p, C.c_int, _f32p, _f32p]
+        L.orc_expert_down.argtypes = [_u8p, C.c_int, _f32p, _f32p]
+        L.orc_moe_block_forward.restype = C.c_int
+        L.orc_moe_block_forward.argtypes = [C.POINTER(OrcLayer), C.c_int, _f32p, C.c_void_p, C.c_void_p,
+                                            C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
+        L.orc_moe_block_forward_batched.restype = C.c_int
+        L.orc_moe_block_forward_batched.argtypes = [C.POINTER(OrcLayer), C.c_int, C.c_int, _f32p, C.c_void_p,
+                                                    _f32p, C.c_void_p, C.c_void_p]
+        L.orc_set_threads.argtypes = [C.c_int]
+        L.orc_get_threads.restype = C.c_int
+        _lib = L
+    return _lib
+
+
+def ref_lib():
+    """The reference's src/math.m compiled as C, or None when it was not built here."""
+    if not os.path.exists(REF_LIB_PATH):
+        return None
+    L = C.CDLL(REF_LIB_PATH)
+    L.nmoe_cpu_softmax.argtypes = [_f32p, C.c_size_t]
+    L.nmoe_cpu_topk.restype = C.c_size_t
+    L.nmoe_cpu_topk.argtypes = [_f32p, C.c_size_t, C.c_size_t, np.ctypeslib.ndpointer(np.uint64), _f32p]
+    L.nmoe_cpu_renormalize.argtypes = [_f32p, C.c_size_t]
+    L.nmoe_cpu_swiglu.argtypes = [_f32p, _f32p, _f32p, C.c_size_t]
+    L.nmoe_cpu_sigmoid.restype = C.c_float
+    L.nmoe_cpu_sigmoid.argtypes = [C.c_float]
+    L.nmoe_cpu_dequant_matvec.argtypes = [_u32p, _u16p, _u16p, _f32p, _f32p, C.c_size_t, C.c_size_t, C.c_int]
+    L.nmoe_f32_to_bf16.restype = C.c_uint16
+    L.nmoe_f32_to_bf16.argtypes = [C.c_float]
+    return L
+
+
+class OrcDense(C.Structure):
+    _fields_ = [("dtype", C.c_int), ("weight", C.c_void_p), ("scales", C.c_void_p), ("biases", C.c_void_p)]
+
+
+class OrcLayer(C.Structure):
+    _fields_ = [("bits", C.c_int), ("experts", C.c_void_p), ("num_experts", C.c_size_t),
+                ("router", OrcDense), ("shared_gate", OrcDense), ("shared_up", OrcDense),
+                ("shared_down", OrcDense), ("shared_gate_vec", OrcDense)]
+
+
+# ------------------------------------------------------------------ helpers ----
+
+def f32_to_bf16(a: np.ndarray) -> np.ndarray:
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    u = a.view(np.uint32)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+def bf16_to_f32(a: np.ndarray) -> np.ndarray:
+    return (np.ascontiguousarray(a, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def quantize_rows(rows_bf16: np.ndarray, bits: int):
+    rows_bf16 = np.ascontiguousarray(rows_bf16, dtype=np.uint16)
+    r, c = rows_bf16.shape
+    packed = np.zeros((r, c * bits // 32), np.uint32)
+    scales = np.zeros((r, c // GROUP), np.uint16)
+    biases = np.zeros((r, c // GROUP), np.uint16)
+    rc = lib().orc_quantize_rows(rows_bf16, r, c, bits, packed, scales, biases)
+    if rc != 0:
+        raise ValueError("orc_quantize_rows failed")
+    return packed, scales, biases
+
+
+def expert_size(bits: int) -> int:
+    return int(lib().orc_expert_size(bits))
+
+
+def expert_offsets(bits: int):
+    arr = (C.c_size_t * 9)()
+    if lib().orc_expert_offsets(bits, arr) != 0:
+        raise ValueError(bits)
+    return [int(v) for v in arr]
+
+
+def pack_expert(gate_up_bf16: np.ndarray, down_bf16: np.ndarray, bits: int) -> np.ndarray:
+    blob = np.zeros(expert_size(bits), np.uint8)
+    rc = lib().orc_pack_expert(np.ascontiguousarray(gate_up_bf16, np.uint16),
+                               np.ascontiguousarray(down_bf16, np.uint16), bits, blob)
+    if rc != 0:
+        raise ValueError("orc_pack_expert failed")
+    return blob
+
+
+def randn_bf16(rng: np.random.Generator, shape, std: float) -> np.ndarray:
+    return f32_to_bf16(rng.standard_normal(shape, dtype=np.float32) * np.float32(std))
+
+
+def _dense_bf16_or_q4(rng, shape, dtype, std=0.02):
+    w = randn_bf16(rng, shape, std)
+    if dtype == DTYPE_BF16:
+        return {"dtype": DTYPE_BF16, "weight": w}
+    p, s, b = quantize_rows(w, 4)
+    return {"dtype": DTYPE_Q4, "weight": p, "scales": s, "biases": b}
+
+
+@dataclass
+class LayerWeights:
+    """One synthetic MoE layer: expert packs (layer_XX.bin image) + router/shared weights."""
+    bits: int
+    experts: np.ndarray          # uint8 [num_experts * expert_size]
+    num_experts: int
+    router: dict
+    shared_gate: dict
+    shared_up: dict
+    shared_down: dict
+    shared_gate_vec: dict
+    router_bias: np.ndarray | None = None   # optional per-expert logit offset (skewed routing)
+    _keep: list = field(default_factory=list)
+
+    def orc(self) -> OrcLayer:
+        def dense(d):
+            out = OrcDense(d["dtype"], d["weight"].ctypes.data, 0, 0)
+            if d["dtype"] == DTYPE_Q4:
+                out.scales = d["scales"].ctypes.data
+                out.biases = d["biases"].ctypes.data
+            return out
+        L = OrcLayer(self.bits, self.experts.ctypes.data, self.num_experts, dense(self.router),
+                     dense(self.shared_gate), dense(self.shared_up), dense(self.shared_down),
+                     dense(self.shared_gate_vec))
+        return L
+
+
+def make_layer(seed: int, bits: int = 4, router_dtype: int = DTYPE_BF16, shared_dtype: int = DTYPE_BF16,
+               num_experts: int = EXPERTS, distinct_experts: int | None = None) -> LayerWeights:
+    """Seeded synthetic layer (BASELINE config 0/1 distributions).
+
+    Experts: gate_up [1024,2048] and down [2048,512] bf16 ~N(0,0.02) quantised by the
+    restated convert_qwen36.py quantiser.  `distinct_experts` (default: all) bounds the
+    host cost: expert e reuses the pack of e % distinct_experts (tests use this to stay
+    fast; routing still addresses all `num_experts` slots).
+    """
+    rng = np.random.default_rng(seed)
+    esz = expert_size(bits)
+    nd = num_experts if distinct_experts is None else max(1, min(distinct_experts, num_experts))
+    packs = []
+    for _ in range(nd):
+        gu = randn_bf16(rng, (2 * INTER, HIDDEN), 0.02)
+        dn = randn_bf16(rng, (HIDDEN, INTER), 0.02)
+        packs.append(pack_expert(gu, dn, bits))
+    experts = np.empty(num_experts * esz, np.uint8)
+    for e in range(num_experts):
+        experts[e * esz:(e + 1) * esz] = packs[e % nd]
+    return LayerWeights(
+        bits=bits, experts=experts, num_experts=num_experts,
+        router=_dense_bf16_or_q4(rng, (EXPERTS, HIDDEN), router_dtype),
+        shared_gate=_dense_bf16_or_q4(rng, (INTER, HIDDEN), shared_dtype),
+        shared_up=_dense_bf16_or_q4(rng, (INTER, HIDDEN), shared_dtype),
+        shared_down=_dense_bf16_or_q4(rng, (HIDDEN, INTER), shared_dtype),
+        shared_gate_vec=_dense_bf16_or_q4(rng, (1, HIDDEN), shared_dtype),
+    )
+
+
+def block_forward(layer: LayerWeights, k: int, x: np.ndarray, h_mid: np.ndarray | None = None,
+                  logits_override: np.ndarray | None = None):
+    """One token through the oracle block. Returns dict(out, idx, w, logits, shared_act, score)."""
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.zeros(HIDDEN, np.float32)
+    idx = np.zeros(MAX_K, np.uint32)
+    w = np.zeros(MAX_K, np.float32)
+    logits = np.zeros(EXPERTS, np.float32)
+    sact = np.zeros(INTER, np.float32)
+    score = np.zeros(1, np.float32)
+    hm = None if h_mid is None else np.ascontiguousarray(h_mid, np.float32)
+    lo = None if logits_override is None else np.ascontiguousarray(logits_override, np.float32)
+    L = layer.orc()
+    rc = lib().orc_moe_block_forward(C.byref(L), k, x, None if hm is None else hm.ctypes.data,
+                                     None if lo is None else lo.ctypes.data, out.ctypes.data,
+                                     idx.ctypes.data, w.ctypes.data, logits.ctypes.data,
+                                     sact.ctypes.data, score.ctypes.data)
+    if rc != 0:
+        raise ValueError(f"orc_moe_block_forward rc={rc}")
+    return {"out": out, "idx": idx, "w": w, "logits": logits, "shared_act": sact, "score": float(score[0])}
+
+
+def block_forward_batched(layer: LayerWeights, k: int, x: np.ndarray, h_mid: np.ndarray | None = None):
+    x = np.ascontiguousarray(x, np.float32)
+    T = x.shape[0]
+    out = np.zeros((T, HIDDEN), np.float32)
+    idx = np.zeros((T, MAX_K), np.uint32)
+    w = np.zeros((T, MAX_K), np.float32)
+    hm = None if h_mid is None else np.ascontiguousarray(h_mid, np.float32)
+    L = layer.orc()
+    rc = lib().orc_moe_block_forward_batched(C.byref(L), T, k, x, None if hm is None else hm.ctypes.data,
+                                             out, idx.ctypes.data, w.ctypes.data)
+    if rc != 0:
+        raise ValueError(f"orc_moe_block_forward_batched rc={rc}")
+    return {"out": out, "idx": idx, "w": w}
+
+
+def route_reference(logits: np.ndarray, k: int):
+    """Softmax -> top-k -> renormalise exactly as NMOESelectRouteTopKCPU (src/runtime.m:1498-1511)."""
+    p = np.array(logits, np.float32, copy=True)
+    L = lib()
+    L.orc_softmax(p, p.size)
+    idx = np.zeros(k, np.uint32)
+    vals = np.zeros(k, np.float32)
+    n = L.orc_topk(p, p.size, k, idx, vals)
+    L.orc_renormalize(vals, n)
+    return idx[:n], vals[:n]
