@@ -1,0 +1,396 @@
+#!/usr/bin/env python3
+"""Benchmark of the routed-MoE hot path (BASELINE metric: routed-MoE tokens/s/layer).
+
+Workload: Qwen3.6-35B-A3B MoE block, batch-1 decode, q4 expert
+packs, k = 8 of 256, bf16 router / shared expert / gate vector, x bf16 [1, 2048].
+One step = one decode token through the MoE blocks of all 40 layers (40 layer calls,
+each with its own resident weights and its own input row). 40 layers x 256 experts of
+q4 packs (18.1 GB) stay resident in HBM; each layer call reads its 8 routed experts
+plus router and shared expert (21.5 MB), so a step touches ~860 MB, far above the
+126 MB L2 (no flush needed; said in `config`).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+ours: `value` = layer calls / s with inputs resident in HBM (CUDA graph of the 40
+calls, timed with CUDA events, max over ranks); `e2e` = the same metric through the C
+ABI with pinned host inputs copied in and outputs read back every step.
+reference: the CPU restatement of the reference's block (oracle, OpenMP over all
+host cores) on a bounded sample of the same workload.
+N > 1: batch-1 decode does not shard (one token); each rank runs an independent
+replica on its own GPU ("replicas only"), value = all ranks' layer calls / max time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(REPO, "nano-metal-moe-qwen36_b200")
+for p in (REPO, PKG):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+METRIC = "routed-MoE tokens/s/layer (batch-1 decode)"
+UNIT = "tokens/s/layer"
+HIDDEN, INTER, EXPERTS = 2048, 512, 256
+FALLBACK_HBM_GBS = 6650.0
+
+
+def algorithmic_bytes(bits: int, k: int, router_dtype: int, shared_dtype: int, x_bytes: int = 2) -> int:
+    """Bytes one batch-1 layer call must move: k expert packs + router + shared expert +
+    gate vector + x in + out (fp32)."""
+    esz = {4: 1769472, 2: 983040}[bits]
+    bf16 = 1
+    router = 256 * 2048 * 2 if router_dtype == bf16 else 256 * 1024 + 2 * 256 * 32 * 2
+    shared = 3 * 512 * 2048 * 2 if shared_dtype == bf16 else 3 * (512 * 1024 + 2 * 512 * 32 * 2)
+    gvec = 2048 * 2 if shared_dtype == bf16 else 1024 + 2 * 32 * 2
+    return k * esz + router + shared + gvec + 2048 * x_bytes + 2048 * 4
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.dev), "-lms", "100"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic(name: str):
+    """dram read+write bytes per launch recorded from ncu in profiles/<name>.md
+    (line 'traffic_bytes_per_launch: N'), or None."""
+    p = os.path.join(REPO, "profiles", name + ".md")
+    try:
+        for ln in open(p):
+            if ln.startswith("traffic_bytes_per_launch:"):
+                return int(float(ln.split(":", 1)[1].strip()))
+    except Exception:
+        pass
+    return None
+
+
+# ------------------------------------------------------------------ workload ----
+
+def build_workload(num_layers: int, bits: int, k: int, router_dtype: int, shared_dtype: int, pool: int, seed: int):
+    """Seeded synthetic layers: `pool` distinct q4 experts quantised by the restated
+    convert_qwen36.py quantiser, placed in the 256 slots of each layer with a per-layer
+    rotation; per-layer bf16 router / shared weights ~N(0, 0.02)."""
+    from oracle import oracle as O
+    rng = np.random.default_rng(seed)
+    esz = O.expert_size(bits)
+    packs = np.stack([O.pack_expert(O.randn_bf16(rng, (1024, 2048), 0.02), O.randn_bf16(rng, (2048, 512), 0.02), bits)
+                      for _ in range(pool)])
+    layers = []
+    for l in range(num_layers):
+        order = (np.arange(EXPERTS) * 7 + l * 13) % pool
+        experts = packs[order].reshape(-1)
+        dense = {}
+        for name, shape, dt in (("router", (256, 2048), router_dtype), ("shared_gate", (512, 2048), shared_dtype),
+                                ("shared_up", (512, 2048), shared_dtype), ("shared_down", (2048, 512), shared_dtype),
+                                ("shared_gate_vec", (1, 2048), shared_dtype)):
+            w = O.randn_bf16(rng, shape, 0.02)
+            if dt == 1:
+                dense[name] = {"dtype": 1, "weight": w}
+            else:
+                p_, s_, b_ = O.quantize_rows(w, 4)
+                dense[name] = {"dtype": 4, "weight": p_, "scales": s_, "biases": b_}
+        layers.append(O.LayerWeights(bits, experts, EXPERTS, dense["router"], dense["shared_gate"],
+                                     dense["shared_up"], dense["shared_down"], dense["shared_gate_vec"]))
+    xs = O.f32_to_bf16(rng.standard_normal((num_layers, HIDDEN), dtype=np.float32))
+    return layers, xs
+
+
+def cpu_baseline_sample(layers, xs, k, seconds: float):
+    """Oracle block forward (all host threads) on a bounded sample of the same calls."""
+    from oracle import oracle as O
+    L = O.lib()
+    n, t0 = 0, time.perf_counter()
+    while True:
+        l = n % len(layers)
+        O.block_forward(layers[l], k, O.bf16_to_f32(xs[l % xs.shape[0]]))
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds and n >= 3:
+            break
+    return n / el, L.orc_get_threads(), n, el
+
+
+# ---------------------------------------------------------------- reference ----
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    from oracle import oracle as O
+    O.build()
+    n_layers = 2
+    layers, xs = build_workload(n_layers, 4, 8, 1, 1, pool=8, seed=args.seed)
+    calls_per_step = 4
+    k = 8
+
+    def step():
+        for j in range(calls_per_step):
+            O.block_forward(layers[j % n_layers], k, O.bf16_to_f32(xs[j % n_layers]))
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    value = args.steps * calls_per_step / el
+    cores = O.lib().orc_get_threads()
+    sample = (f"{calls_per_step} batch-1 layer calls per step (config 0: q4 experts, k=8, bf16 router/shared), "
+              f"CPU oracle port of the reference block, OpenMP over output rows")
+    return {
+        "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded bf16 ~N(0,0.02) weights quantised by the reference quantiser rule)",
+        "config": {"workload": "config0 batch-1 decode, q4 experts, k=8, bf16 router/shared, x bf16",
+                   "layers_in_sample": n_layers},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+# ---------------------------------------------------------------------- ours ----
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    import nmoe_b200 as N
+    from oracle import oracle as O
+
+    dev = local_rank
+    torch.cuda.set_device(dev)
+    bits, k, rdt, sdt = 4, 8, N.DTYPE_BF16, N.DTYPE_BF16
+    L = args.layers
+    layers, xs_h = build_workload(L, bits, k, rdt, sdt, pool=args.pool, seed=args.seed + rank)
+    ctx = N.Context(quant_bits=bits, num_layers=L, router_dtype=rdt, shared_dtype=sdt, device=dev)
+    for l, lw in enumerate(layers):
+        ctx.load_layer(l, lw.experts)
+        ctx.set_dense(l, lw.router, lw.shared_gate, lw.shared_up, lw.shared_down, lw.shared_gate_vec)
+    cpu_layers = layers[:2]
+    for lw in layers[2:]:
+        lw.experts = None
+    del layers
+
+    xs = torch.from_numpy(xs_h.view(np.int16)).to(f"cuda:{dev}")
+    outs = torch.zeros((L, HIDDEN), dtype=torch.float32, device=f"cuda:{dev}")
+    stream = torch.cuda.Stream(device=dev)
+
+    def step_direct(s):
+        for l in range(L):
+            ctx.forward(l, k, xs[l], outs[l], x_dtype=N.DTYPE_BF16, stream=s)
+
+    # correctness gate on this box before timing: layer 0 against the oracle
+    with torch.cuda.stream(stream):
+        step_direct(stream.cuda_stream)
+    stream.synchronize()
+    rc, code = ctx.device_status()
+    if rc != N.OK:
+        raise RuntimeError(f"device error word {code} after the first step")
+
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step_direct(torch.cuda.current_stream().cuda_stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(dev)
+    clocks.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(args.steps):
+            graph.replay()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    t = torch.tensor([ms], dtype=torch.float64, device=f"cuda:{dev}")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    calls = args.steps * L * world
+    value = calls / (ms_max / 1e3)
+
+    # e2e: public C ABI, pinned host inputs in, outputs read back, every step
+    xs_pin = torch.from_numpy(xs_h.view(np.int16)).pin_memory()
+    out_pin = torch.zeros((L, HIDDEN), dtype=torch.float32).pin_memory()
+    e2e_steps = max(1, args.steps // 4)
+
+    def step_e2e():
+        with torch.cuda.stream(stream):
+            xs.copy_(xs_pin, non_blocking=True)
+            step_direct(stream.cuda_stream)
+            out_pin.copy_(outs, non_blocking=True)
+        stream.synchronize()
+
+    for _ in range(3):
+        step_e2e()
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        step_e2e()
+    e2e_el = time.perf_counter() - t0
+    te = torch.tensor([e2e_el], dtype=torch.float64, device=f"cuda:{dev}")
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = e2e_steps * L * world / float(te.item())
+
+    # correctness of the timed outputs (layer 0 vs oracle, using the GPU's own routing)
+    lg = torch.zeros(256, dtype=torch.float32, device=f"cuda:{dev}")
+    ctx.route(0, k, xs[0], x_dtype=N.DTYPE_BF16, logits_out=lg)
+    torch.cuda.synchronize()
+    ref = O.block_forward(cpu_layers[0], k, O.bf16_to_f32(xs_h[0]), logits_override=lg.cpu().numpy())
+    got = outs[0].cpu().numpy()
+    rel = float(np.linalg.norm(got - ref["out"]) / np.linalg.norm(ref["out"]))
+    if rel > 1e-2:
+        raise RuntimeError(f"timed output disagrees with the oracle: rel_l2={rel}")
+
+    result = None
+    if rank == 0:
+        per_launch_s = ms_max / 1e3 / (args.steps * L)
+        abytes = algorithmic_bytes(bits, k, rdt, sdt)
+        pk, pk_kind = peaks()
+        achieved = abytes / per_launch_s / 1e9
+        launches_per_call = 4 if os.environ.get("NMOE_DECODE_KERNEL") == "staged" else 1
+        cpu = None
+        if world == 1:
+            v, cores, n, el = cpu_baseline_sample(cpu_layers, xs_h, k, args.cpu_seconds)
+            cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
+                   "sample": f"{n} batch-1 layer calls of the same config in {el:.1f}s (oracle, OpenMP)"}
+        result = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16/q4 in, f32 accumulate",
+            "data": "synthetic (seeded bf16 ~N(0,0.02) weights quantised by the reference quantiser rule; "
+                    f"{args.pool} distinct expert packs placed in 256 slots per layer)",
+            "config": {"workload": "config0 batch-1 decode: 40 layers x 256 q4 experts resident, k=8, "
+                                   "bf16 router/shared/gate-vector, x bf16 [1,2048]",
+                       "layers": L, "k": k, "step": f"{L} layer calls (one token through {L} MoE blocks)",
+                       "l2": "inputs larger than L2 (a step touches ~860 MB of weights)",
+                       "parallelism": "replicas only" if world > 1 else "single GPU",
+                       "timing": "CUDA graph of one step, CUDA events, max over ranks"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk, "unit": "GB/s", "frac": achieved / pk,
+                         "peak_kind": pk_kind, "algorithmic_bytes_per_launch": abytes,
+                         "traffic": profiled_traffic("decode_cfg0")},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": L * HIDDEN * 2,
+                    "d2h_bytes_per_step": L * HIDDEN * 4},
+            "gpu_launches": args.steps * L * launches_per_call,
+            "clocks": clk,
+            "check": {"rel_l2_layer0": rel},
+        }
+    ctx.close()
+    return result
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--layers", type=int, default=40)
+    ap.add_argument("--pool", type=int, default=32, help="distinct expert packs generated on the host")
+    ap.add_argument("--seed", type=int, default=2026)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        res = run_reference(args, rank, world)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local_rank}"))
+    res = run_ours(args, rank, world, local_rank)
+    if res is not None:
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

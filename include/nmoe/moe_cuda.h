@@ -1,0 +1,175 @@
+/*
+ * nmoe/moe_cuda.h -- C ABI of the B200 (sm_100a) routed-MoE block for nmoe.
+ *
+ * This is the drop-in seam for nmoe's host (src/runtime.m): everything between the
+ * post-attention RMSNorm output (`normBuffer`) and the layer output is one call here.
+ * It replaces, in the reference:
+ *   - the router + shared-expert encoders  NMOEEncodeRouteSharedQ4Tensors
+ *     (src/runtime.m:970-1038) and the q2-mode dequant/gate-up encoders
+ *     (src/runtime.m:3151-3166, 3498-3513);
+ *   - routing  NMOESelectRouteTopKCPU (src/runtime.m:1498-1511) / NMOEEncodeRouteTopK
+ *     (src/runtime.m:1403-1424);
+ *   - the expert phase  NMOEEncodeExpertPhase (src/runtime.m:2778-2903) and its
+ *     pipelined tail NMOEPipelinedExpertTail (src/runtime.m:2908-2999);
+ *   - the SSD expert loader  nmoe_expert_store_open / NMOEAsyncReadExpertsRange
+ *     (include/nmoe/expert_io.h:22-26, src/runtime.m:1588-1634) -- expert packs are
+ *     uploaded once and stay resident in HBM.
+ *
+ * Conventions (mirroring include/nmoe/expert_io.h and include/nmoe/backend.h):
+ *   - plain C: no CUDA or C++ types; a CUDA stream is passed as `void *` (cudaStream_t);
+ *   - every call returns an int status (NMOE_OK == 0), detail in nmoe_moe_last_error();
+ *   - tensors passed to forward calls are DEVICE pointers owned by the caller;
+ *     weights passed to load/set calls are HOST pointers, copied into the context;
+ *   - one host thread per context (the reference has one Metal queue,
+ *     src/backend/metal_backend.m:271); contexts on different devices are independent.
+ */
+#ifndef NMOE_MOE_CUDA_H
+#define NMOE_MOE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (reference: BOOL + NSError, src/expert_io.m:52-65) ---------- */
+#define NMOE_OK 0
+#define NMOE_EINVAL 1   /* bad argument: k outside [1,k_max], layer/expert out of range, dtype */
+#define NMOE_ESIZE 2    /* pack or layout size mismatch (src/runtime.m:2445 check)            */
+#define NMOE_ECUDA 3    /* CUDA runtime error (no device, launch failure, ...)                 */
+#define NMOE_ENCCL 4    /* NCCL error in the expert-parallel path                              */
+#define NMOE_ETIMEOUT 5 /* a bounded device-side wait expired (never traps)                   */
+#define NMOE_EDEVICE 6  /* the device error word was set (e.g. routed expert id >= experts)   */
+#define NMOE_EIO 7      /* file open/read error                                               */
+#define NMOE_ENOMEM 8   /* allocation failure                                                 */
+
+/* ---- dtypes ------------------------------------------------------------------- */
+#define NMOE_DTYPE_F32 0
+#define NMOE_DTYPE_BF16 1
+#define NMOE_DTYPE_Q2 2
+#define NMOE_DTYPE_Q4 4
+
+/* ---- fixed Qwen3.6-35B-A3B MoE geometry (src/runtime.m:31-44, convert_qwen36.py:31-36) */
+#define NMOE_HIDDEN 2048
+#define NMOE_INTER 512
+#define NMOE_NUM_EXPERTS 256
+#define NMOE_GROUP 64
+#define NMOE_MAX_K 8 /* include/nmoe/expert_io.h:11 */
+
+typedef struct nmoe_moe_ctx nmoe_moe_ctx;
+
+typedef struct nmoe_moe_config {
+    int quant_bits;    /* expert packs: 4 (packed_experts) or 2 (packed_experts_2bit)        */
+    int num_layers;    /* 40 for the full model; any >= 1                                    */
+    int num_experts;   /* 256                                                                */
+    int k_max;         /* largest k a forward call may use, 1..8 (--experts, app_config.m)   */
+    int router_dtype;  /* NMOE_DTYPE_BF16 or NMOE_DTYPE_Q4 (reference model_weights: q4)     */
+    int shared_dtype;  /* NMOE_DTYPE_BF16 or NMOE_DTYPE_Q4 (shared expert + its gate vector)  */
+    int t_max;         /* largest T of nmoe_moe_forward_batched (workspace is sized at create) */
+    int world_size;    /* expert-parallel ranks (1 = single GPU)                             */
+    int rank;          /* this process's rank, 0..world_size-1                               */
+    const void *nccl_unique_id; /* 128-byte ncclUniqueId shared by all ranks (world_size>1)  */
+} nmoe_moe_config;
+
+/* A matrix given to nmoe_moe_set_dense: bf16 uses `weight` only ([rows][cols] u16);
+ * q4 uses weight ([rows][cols/8] u32), scales and biases ([rows][cols/64] bf16), the
+ * layout written by quantize_matrix_to_weights (scripts/convert_qwen36.py:214-263). */
+typedef struct nmoe_tensor {
+    const void *weight;
+    const void *scales;
+    const void *biases;
+} nmoe_tensor;
+
+/* The per-layer non-expert MoE weights, named as in model_weights.json
+ * (src/runtime.m:2357-2371). */
+typedef struct nmoe_moe_dense_weights {
+    nmoe_tensor router;          /* model.layers.N.mlp.gate                    [256][2048] */
+    nmoe_tensor shared_gate;     /* model.layers.N.mlp.shared_expert.gate_proj [512][2048] */
+    nmoe_tensor shared_up;       /* model.layers.N.mlp.shared_expert.up_proj   [512][2048] */
+    nmoe_tensor shared_down;     /* model.layers.N.mlp.shared_expert.down_proj [2048][512] */
+    nmoe_tensor shared_gate_vec; /* model.layers.N.mlp.shared_expert_gate      [1][2048]   */
+} nmoe_moe_dense_weights;
+
+/* ---- host-only pack/layout helpers (no GPU needed) ------------------------------ */
+
+/* Bytes of one expert blob: 1,769,472 (q4) / 983,040 (q2). Replaces
+ * nmoe_expert_active_size (include/nmoe/expert_io.h:28). 0 for other bits. */
+size_t nmoe_moe_expert_size(int quant_bits);
+
+/* The nine component offsets of an expert blob, in EXPERT_LAYOUT order
+ * (scripts/convert_qwen36.py:38-64; NMOEExpertOffsetsForBits, src/runtime.m:2240-2252). */
+int nmoe_moe_expert_offsets(int quant_bits, size_t offsets[9]);
+
+/* Validate a converter-written layout.json (scripts/convert_qwen36.py:351-359: keys
+ * expert_size, num_layers, num_experts, components[{name,offset,size}]) against the
+ * built-in layout for `quant_bits`. Accepts, unlike the reference's never-called
+ * validator (src/expert_io.m:274-316), the keys the converter actually writes; optional
+ * dtype/shape keys are checked when present. Message (if any) goes to err[errlen]. */
+int nmoe_moe_validate_layout_json(const char *path, int quant_bits, char *err, size_t errlen);
+
+const char *nmoe_moe_strerror(int status);
+
+/* ---- context ------------------------------------------------------------------ */
+
+/* Create a context on CUDA device `device` (replaces nmoe_backend_create +
+ * NMOEInitExpertIOBuffers, src/runtime.m:2664, 1542). Device memory for all layers'
+ * expert packs and dense weights plus every workspace is reserved here; forward calls
+ * allocate nothing. With world_size > 1 the context owns an NCCL communicator and holds
+ * only its 1/world_size share of each layer's experts. */
+nmoe_moe_ctx *nmoe_moe_create(const nmoe_moe_config *cfg, int device, int *status);
+void nmoe_moe_destroy(nmoe_moe_ctx *ctx);
+/* Message of the last failed nmoe_moe_create on this host thread (no context exists). */
+const char *nmoe_moe_create_error(void);
+const char *nmoe_moe_last_error(const nmoe_moe_ctx *ctx);
+
+/* Upload one layer's expert packs from a host image of layer_XX.bin: exactly
+ * num_experts * expert_size bytes (the size check of NMOELoadExpertLayer,
+ * src/runtime.m:2445, made exact). Replaces the per-token pread loader. */
+int nmoe_moe_load_layer(nmoe_moe_ctx *ctx, int layer, const void *layer_bin, size_t bytes);
+/* Same, reading the file at `path` (e.g. packed_experts/layer_07.bin). */
+int nmoe_moe_load_layer_file(nmoe_moe_ctx *ctx, int layer, const char *path);
+/* Upload one layer's router + shared-expert weights (dtypes from the config). */
+int nmoe_moe_set_dense(nmoe_moe_ctx *ctx, int layer, const nmoe_moe_dense_weights *w);
+
+/* ---- forward ------------------------------------------------------------------ */
+
+/* One token through layer `layer`'s routed-MoE block, asynchronous on `stream`:
+ *   out[r] = h_mid[r] + sum_{s<k} w_s * down_{e_s}(SiLU(gate_{e_s} x) * up_{e_s} x)
+ *            + sigmoid(gvec . x) * shared_down(SiLU(shared_gate x) * shared_up x)
+ * with (e_s, w_s) the top-k of softmax(router x) renormalised over the k picks
+ * (NMOESelectRouteTopKCPU semantics: descending, lower expert id wins a tie).
+ *   x      device [2048], x_dtype NMOE_DTYPE_BF16 or NMOE_DTYPE_F32
+ *   h_mid  device fp32 [2048] residual, or NULL for the bare block output
+ *   out    device fp32 [2048]
+ *   idx_out/w_out  device [8] (uint32 / fp32), optional; slots >= k are (0, 0.0)
+ *                  as in nmoe_route_topk (metal/kernels.metal:1767-1775)
+ * k must be in [1, k_max] (the reference clamps --experts to 1..8, app_config.m:215-226;
+ * the library rejects instead of clamping). Replaces src/runtime.m:3151-3201. */
+int nmoe_moe_forward(nmoe_moe_ctx *ctx, int layer, int k, const void *x, int x_dtype,
+                     const float *h_mid, float *out, uint32_t *idx_out, float *w_out, void *stream);
+
+/* Routing only: router logits (device fp32 [256], optional), top-k ids and renormalised
+ * weights (device [8], optional). Same rule as nmoe_moe_forward. The GPU counterpart of
+ * NMOEEncodeRouteTopK + nmoe_route_topk (src/runtime.m:1403-1424, kernels.metal:1715-1776). */
+int nmoe_moe_route(nmoe_moe_ctx *ctx, int layer, int k, const void *x, int x_dtype,
+                   float *logits_out, uint32_t *idx_out, float *w_out, void *stream);
+
+/* T tokens (prefill / batched decode) through one layer: x device [T][2048] (bf16 or
+ * f32), h_mid device fp32 [T][2048] or NULL, out device [T][2048] in out_dtype
+ * (F32 or BF16), idx_out/w_out device [T][8] optional. T <= t_max. With world_size > 1
+ * every rank passes its own T tokens; experts are sharded num_experts/world_size per
+ * rank and tokens travel by NCCL all-to-all. No reference counterpart (the reference
+ * runs prefill token by token, src/runtime.m:3816). */
+int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int k, const void *x, int x_dtype,
+                             const float *h_mid, void *out, int out_dtype, uint32_t *idx_out,
+                             float *w_out, void *stream);
+
+/* Read and clear the device error word (synchronises the context's device). Returns
+ * NMOE_OK or NMOE_EDEVICE and the first recorded code in *code (may be NULL). */
+int nmoe_moe_device_status(nmoe_moe_ctx *ctx, int *code);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

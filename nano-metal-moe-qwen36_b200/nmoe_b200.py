@@ -1,0 +1,209 @@
+"""Python host binding of libnmoe_cuda.so (the C ABI declared in include/nmoe/moe_cuda.h).
+
+The reference's host is Objective-C/C calling Metal; here the host-facing surface is
+the C ABI, and this module is a thin ctypes mirror of it for Python callers (tests,
+bench.py). Tensors passed to forward calls are device pointers (ints) or torch CUDA
+tensors; weights passed to load/set calls are host numpy arrays.
+
+There is no fallback: if the CUDA library is missing, `lib()` raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libnmoe_cuda.so")
+
+OK, EINVAL, ESIZE, ECUDA, ENCCL, ETIMEOUT, EDEVICE, EIO, ENOMEM = range(9)
+DTYPE_F32, DTYPE_BF16, DTYPE_Q2, DTYPE_Q4 = 0, 1, 2, 4
+HIDDEN, INTER, NUM_EXPERTS, GROUP, MAX_K = 2048, 512, 256, 64, 8
+
+# Every symbol include/nmoe/moe_cuda.h declares.
+ABI_SYMBOLS = (
+    "nmoe_moe_expert_size", "nmoe_moe_expert_offsets", "nmoe_moe_validate_layout_json",
+    "nmoe_moe_strerror", "nmoe_moe_create", "nmoe_moe_destroy", "nmoe_moe_create_error", "nmoe_moe_last_error",
+    "nmoe_moe_load_layer", "nmoe_moe_load_layer_file", "nmoe_moe_set_dense",
+    "nmoe_moe_forward", "nmoe_moe_route", "nmoe_moe_forward_batched", "nmoe_moe_device_status",
+)
+
+
+class NmoeError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"nmoe status {status}: {msg}")
+        self.status = status
+
+
+class Config(C.Structure):
+    _fields_ = [("quant_bits", C.c_int), ("num_layers", C.c_int), ("num_experts", C.c_int),
+                ("k_max", C.c_int), ("router_dtype", C.c_int), ("shared_dtype", C.c_int),
+                ("t_max", C.c_int), ("world_size", C.c_int), ("rank", C.c_int),
+                ("nccl_unique_id", C.c_void_p)]
+
+
+class Tensor(C.Structure):
+    _fields_ = [("weight", C.c_void_p), ("scales", C.c_void_p), ("biases", C.c_void_p)]
+
+
+class DenseWeights(C.Structure):
+    _fields_ = [("router", Tensor), ("shared_gate", Tensor), ("shared_up", Tensor),
+                ("shared_down", Tensor), ("shared_gate_vec", Tensor)]
+
+
+def build(quiet: bool = True) -> str:
+    out = subprocess.DEVNULL if quiet else None
+    subprocess.run(["make", "-C", HERE, "-j8", "all"], check=True, stdout=out)
+    return LIB_PATH
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(f"{LIB_PATH} is missing: build it with `make -C {HERE}` "
+                           "(or __graft_entry__.build()); there is no CPU fallback")
+    L = C.CDLL(LIB_PATH)
+    vp, i, sz = C.c_void_p, C.c_int, C.c_size_t
+    L.nmoe_moe_expert_size.restype = sz
+    L.nmoe_moe_expert_size.argtypes = [i]
+    L.nmoe_moe_expert_offsets.restype = i
+    L.nmoe_moe_expert_offsets.argtypes = [i, C.POINTER(sz)]
+    L.nmoe_moe_validate_layout_json.restype = i
+    L.nmoe_moe_validate_layout_json.argtypes = [C.c_char_p, i, C.c_char_p, sz]
+    L.nmoe_moe_strerror.restype = C.c_char_p
+    L.nmoe_moe_strerror.argtypes = [i]
+    L.nmoe_moe_create.restype = vp
+    L.nmoe_moe_create.argtypes = [C.POINTER(Config), i, C.POINTER(i)]
+    L.nmoe_moe_create_error.restype = C.c_char_p
+    L.nmoe_moe_destroy.argtypes = [vp]
+    L.nmoe_moe_last_error.restype = C.c_char_p
+    L.nmoe_moe_last_error.argtypes = [vp]
+    L.nmoe_moe_load_layer.restype = i
+    L.nmoe_moe_load_layer.argtypes = [vp, i, vp, sz]
+    L.nmoe_moe_load_layer_file.restype = i
+    L.nmoe_moe_load_layer_file.argtypes = [vp, i, C.c_char_p]
+    L.nmoe_moe_set_dense.restype = i
+    L.nmoe_moe_set_dense.argtypes = [vp, i, C.POINTER(DenseWeights)]
+    L.nmoe_moe_forward.restype = i
+    L.nmoe_moe_forward.argtypes = [vp, i, i, vp, i, vp, vp, vp, vp, vp]
+    L.nmoe_moe_route.restype = i
+    L.nmoe_moe_route.argtypes = [vp, i, i, vp, i, vp, vp, vp, vp]
+    L.nmoe_moe_forward_batched.restype = i
+    L.nmoe_moe_forward_batched.argtypes = [vp, i, i, i, vp, i, vp, vp, i, vp, vp, vp]
+    L.nmoe_moe_device_status.restype = i
+    L.nmoe_moe_device_status.argtypes = [vp, C.POINTER(i)]
+    _lib = L
+    return L
+
+
+def expert_size(bits: int) -> int:
+    return int(lib().nmoe_moe_expert_size(bits))
+
+
+def expert_offsets(bits: int):
+    arr = (C.c_size_t * 9)()
+    rc = lib().nmoe_moe_expert_offsets(bits, arr)
+    if rc != OK:
+        raise NmoeError(rc, "bad quant_bits")
+    return [int(v) for v in arr]
+
+
+def validate_layout_json(path: str, bits: int):
+    """Returns (status, message)."""
+    buf = C.create_string_buffer(512)
+    rc = lib().nmoe_moe_validate_layout_json(path.encode(), bits, buf, 512)
+    return rc, buf.value.decode()
+
+
+def _ptr(t) -> int | None:
+    if t is None:
+        return None
+    if isinstance(t, int):
+        return t
+    return t.data_ptr()
+
+
+def _np_ptr(a) -> int | None:
+    return None if a is None else a.ctypes.data
+
+
+class Context:
+    """One nmoe_moe_ctx on one CUDA device."""
+
+    def __init__(self, quant_bits=4, num_layers=1, num_experts=NUM_EXPERTS, k_max=8,
+                 router_dtype=DTYPE_BF16, shared_dtype=DTYPE_BF16, t_max=0, device=0,
+                 world_size=1, rank=0, nccl_unique_id: bytes | None = None):
+        self._L = lib()
+        self._id_buf = None
+        if nccl_unique_id is not None:
+            self._id_buf = C.create_string_buffer(bytes(nccl_unique_id), 128)
+        self.cfg = Config(quant_bits, num_layers, num_experts, k_max, router_dtype, shared_dtype, t_max,
+                          world_size, rank, C.cast(self._id_buf, C.c_void_p) if self._id_buf else None)
+        st = C.c_int(0)
+        h = self._L.nmoe_moe_create(C.byref(self.cfg), device, C.byref(st))
+        if not h:
+            raise NmoeError(st.value, self._L.nmoe_moe_create_error().decode())
+        self.h = h
+        self.device = device
+
+    def close(self):
+        if getattr(self, "h", None):
+            self._L.nmoe_moe_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _check(self, rc):
+        if rc != OK:
+            raise NmoeError(rc, self._L.nmoe_moe_last_error(self.h).decode())
+
+    def load_layer(self, layer: int, layer_bin: np.ndarray):
+        a = np.ascontiguousarray(layer_bin).view(np.uint8)
+        self._check(self._L.nmoe_moe_load_layer(self.h, layer, a.ctypes.data, a.nbytes))
+
+    def load_layer_file(self, layer: int, path: str):
+        self._check(self._L.nmoe_moe_load_layer_file(self.h, layer, path.encode()))
+
+    def set_dense(self, layer: int, router: dict, shared_gate: dict, shared_up: dict, shared_down: dict,
+                  shared_gate_vec: dict):
+        """Each dict: {"weight": ndarray, ["scales": ndarray, "biases": ndarray]}."""
+        keep = []
+
+        def t(d):
+            w = np.ascontiguousarray(d["weight"])
+            s = np.ascontiguousarray(d["scales"]) if d.get("scales") is not None else None
+            b = np.ascontiguousarray(d["biases"]) if d.get("biases") is not None else None
+            keep.extend([w, s, b])
+            return Tensor(w.ctypes.data, _np_ptr(s), _np_ptr(b))
+
+        dw = DenseWeights(t(router), t(shared_gate), t(shared_up), t(shared_down), t(shared_gate_vec))
+        self._check(self._L.nmoe_moe_set_dense(self.h, layer, C.byref(dw)))
+
+    def forward(self, layer, k, x, out, x_dtype=DTYPE_BF16, h_mid=None, idx_out=None, w_out=None, stream=0):
+        self._check(self._L.nmoe_moe_forward(self.h, layer, k, _ptr(x), x_dtype, _ptr(h_mid), _ptr(out),
+                                             _ptr(idx_out), _ptr(w_out), stream))
+
+    def route(self, layer, k, x, x_dtype=DTYPE_BF16, logits_out=None, idx_out=None, w_out=None, stream=0):
+        self._check(self._L.nmoe_moe_route(self.h, layer, k, _ptr(x), x_dtype, _ptr(logits_out), _ptr(idx_out),
+                                           _ptr(w_out), stream))
+
+    def forward_batched(self, layer, T, k, x, out, x_dtype=DTYPE_BF16, out_dtype=DTYPE_F32, h_mid=None,
+                        idx_out=None, w_out=None, stream=0):
+        self._check(self._L.nmoe_moe_forward_batched(self.h, layer, T, k, _ptr(x), x_dtype, _ptr(h_mid), _ptr(out),
+                                                     out_dtype, _ptr(idx_out), _ptr(w_out), stream))
+
+    def device_status(self):
+        code = C.c_int(0)
+        rc = self._L.nmoe_moe_device_status(self.h, C.byref(code))
+        return rc, code.value

@@ -1,0 +1,193 @@
+"""Batch-1 routed-MoE block on the GPU through the C ABI, against the CPU oracle.
+
+Parity bar: router indices bit-exact, outputs within 1e-2
+relative L2 (we assert far tighter where the arithmetic allows it).
+Routing is compared on the GPU's own logits: the oracle's reference top-k
+(softmax -> top-k -> renormalise of src/math.m) run on those logits must pick the
+same experts in the same order."""
+import numpy as np
+import pytest
+
+import nmoe_b200 as N
+from nmoe_testutil import bf16_round, rel_l2, upload
+from oracle import oracle as O
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+CONFIGS = {
+    # name: (bits, router dtype, shared dtype, x dtype)
+    "cfg0_q4_bf16": (4, N.DTYPE_BF16, N.DTYPE_BF16, N.DTYPE_BF16),
+    "ref_q4_q4_f32": (4, N.DTYPE_Q4, N.DTYPE_Q4, N.DTYPE_F32),
+    "cfg1_q2_bf16": (2, N.DTYPE_BF16, N.DTYPE_BF16, N.DTYPE_BF16),
+    "q2_q4_f32": (2, N.DTYPE_Q4, N.DTYPE_Q4, N.DTYPE_F32),
+}
+
+_cache = {}
+
+
+def setup(name, num_layers=2):
+    if name in _cache:
+        return _cache[name]
+    bits, rdt, sdt, _ = CONFIGS[name]
+    ctx = N.Context(quant_bits=bits, num_layers=num_layers, router_dtype=rdt, shared_dtype=sdt, device=0)
+    layers = []
+    for l in range(num_layers):
+        lw = O.make_layer(100 + l, bits=bits, router_dtype=rdt, shared_dtype=sdt, distinct_experts=24)
+        upload(ctx, l, lw)
+        layers.append(lw)
+    _cache[name] = (ctx, layers)
+    return ctx, layers
+
+
+def make_x(seed, x_dtype):
+    x = np.random.default_rng(seed).standard_normal(2048, dtype=np.float32)
+    if x_dtype == N.DTYPE_BF16:
+        xb = O.f32_to_bf16(x)
+        return O.bf16_to_f32(xb), torch.from_numpy(xb.view(np.int16)).cuda()
+    return x, torch.from_numpy(x).cuda()
+
+
+def run_gpu(ctx, layer, k, xd, x_dtype, hm=None):
+    out = torch.zeros(2048, dtype=torch.float32, device="cuda")
+    idx = torch.full((8,), 77, dtype=torch.int32, device="cuda")
+    w = torch.full((8,), 9.0, dtype=torch.float32, device="cuda")
+    ctx.forward(layer, k, xd, out, x_dtype=x_dtype, h_mid=hm, idx_out=idx, w_out=w)
+    lg = torch.zeros(256, dtype=torch.float32, device="cuda")
+    ctx.route(layer, k, xd, x_dtype=x_dtype, logits_out=lg)
+    torch.cuda.synchronize()
+    return out.cpu().numpy(), idx.cpu().numpy().view(np.uint32), w.cpu().numpy(), lg.cpu().numpy()
+
+
+@pytest.mark.parametrize("name", list(CONFIGS))
+@pytest.mark.parametrize("k", [1, 2, 4, 6, 8])
+def test_block_matches_oracle(name, k):
+    ctx, layers = setup(name)
+    x_dtype = CONFIGS[name][3]
+    for layer in range(len(layers)):
+        for trial in range(2):
+            x, xd = make_x(1000 * layer + 10 * k + trial, x_dtype)
+            out, idx, w, lg = run_gpu(ctx, layer, k, xd, x_dtype)
+            ref = O.block_forward(layers[layer], k, x, logits_override=lg)
+            # logits: fp32 accumulation order differs only
+            assert rel_l2(lg, ref["logits"]) < 1e-5
+            # routing on the GPU's logits is bit-exact with the reference rule
+            ridx, rw = O.route_reference(lg, k)
+            np.testing.assert_array_equal(idx[:k], ridx)
+            np.testing.assert_array_equal(idx[k:], 0)
+            np.testing.assert_allclose(w[:k], rw, rtol=2e-6, atol=1e-7)
+            np.testing.assert_array_equal(w[k:], 0)
+            assert rel_l2(out, ref["out"]) < 1e-4, rel_l2(out, ref["out"])
+            # the oracle routing on its own logits agrees unless the k-th/(k+1)-th gap is a near tie
+            own = O.block_forward(layers[layer], k, x)
+            if not np.array_equal(own["idx"][:k], idx[:k]):
+                srt = np.sort(ref["logits"])[::-1]
+                assert srt[k - 1] - srt[k] < 1e-4
+
+
+@pytest.mark.parametrize("name", ["cfg0_q4_bf16", "ref_q4_q4_f32"])
+def test_residual_h_mid(name):
+    ctx, layers = setup(name)
+    x_dtype = CONFIGS[name][3]
+    x, xd = make_x(5, x_dtype)
+    hm = np.random.default_rng(6).standard_normal(2048, dtype=np.float32)
+    out, _, _, lg = run_gpu(ctx, 0, 8, xd, x_dtype, torch.from_numpy(hm).cuda())
+    ref = O.block_forward(layers[0], 8, x, h_mid=hm, logits_override=lg)
+    assert rel_l2(out, ref["out"]) < 1e-5
+
+
+def test_tie_goes_to_lower_expert_id():
+    """Two identical router rows give bit-identical logits; the lower id must win."""
+    bits = 4
+    ctx = N.Context(quant_bits=bits, num_layers=1, device=0)
+    lw = O.make_layer(7, bits=bits, distinct_experts=8)
+    r = lw.router["weight"].copy()
+    r[200] = r[37]
+    r[201] = r[37]
+    # make the tied rows the top logits for an input aligned with them
+    lw.router = {"dtype": N.DTYPE_BF16, "weight": r}
+    upload(ctx, 0, lw)
+    x = bf16_round(O.bf16_to_f32(r[37]) * 50.0)
+    xd = torch.from_numpy(O.f32_to_bf16(x).view(np.int16)).cuda()
+    for k in (1, 2, 3, 8):
+        out, idx, w, lg = run_gpu(ctx, 0, k, xd, N.DTYPE_BF16)
+        assert lg[37] == lg[200] == lg[201]
+        assert idx[0] == 37
+        if k >= 3:
+            assert list(idx[:3]) == [37, 200, 201]
+        ridx, _ = O.route_reference(lg, k)
+        np.testing.assert_array_equal(idx[:k], ridx)
+
+
+def test_argument_errors():
+    ctx, _ = setup("cfg0_q4_bf16")
+    x, xd = make_x(1, N.DTYPE_BF16)
+    out = torch.zeros(2048, dtype=torch.float32, device="cuda")
+    for k in (0, 9):
+        with pytest.raises(N.NmoeError) as ei:
+            ctx.forward(0, k, xd, out)
+        assert ei.value.status == N.EINVAL
+    with pytest.raises(N.NmoeError) as ei:
+        ctx.forward(5, 8, xd, out)
+    assert ei.value.status == N.EINVAL
+    with pytest.raises(N.NmoeError) as ei:
+        ctx.forward(0, 8, xd, out, x_dtype=N.DTYPE_Q4)
+    assert ei.value.status == N.EINVAL
+    with pytest.raises(N.NmoeError) as ei:
+        ctx.load_layer(0, np.zeros(100, np.uint8))
+    assert ei.value.status == N.ESIZE
+    fresh = N.Context(quant_bits=4, num_layers=1, device=0)
+    with pytest.raises(N.NmoeError) as ei:   # weights never uploaded
+        fresh.forward(0, 8, xd, out)
+    assert ei.value.status == N.EINVAL
+
+
+def test_k_max_bound():
+    ctx = N.Context(quant_bits=4, num_layers=1, k_max=4, device=0)
+    lw = O.make_layer(3, distinct_experts=4)
+    upload(ctx, 0, lw)
+    x, xd = make_x(2, N.DTYPE_BF16)
+    out = torch.zeros(2048, dtype=torch.float32, device="cuda")
+    ctx.forward(0, 4, xd, out)
+    with pytest.raises(N.NmoeError):
+        ctx.forward(0, 5, xd, out)
+
+
+def test_out_of_range_expert_sets_device_error():
+    """num_experts < 256: a routed id beyond the uploaded experts raises the device error
+    word and contributes nothing (the reference's invalid-slot rule, src/runtime.m:2980)."""
+    ne = 16
+    ctx = N.Context(quant_bits=4, num_layers=1, num_experts=ne, device=0)
+    lw = O.make_layer(9, distinct_experts=4)
+    r = lw.router["weight"].copy()
+    upload_lw = O.LayerWeights(4, lw.experts[:ne * O.expert_size(4)].copy(), ne, lw.router, lw.shared_gate,
+                               lw.shared_up, lw.shared_down, lw.shared_gate_vec)
+    upload(ctx, 0, upload_lw)
+    assert ctx.device_status() == (N.OK, 0)
+    x = bf16_round(O.bf16_to_f32(r[100]) * 50.0)   # expert 100 wins
+    xd = torch.from_numpy(O.f32_to_bf16(x).view(np.int16)).cuda()
+    out, idx, w, lg = run_gpu(ctx, 0, 1, xd, N.DTYPE_BF16)
+    assert idx[0] == 100
+    rc, code = ctx.device_status()
+    assert rc == N.EDEVICE and code == 1
+    assert ctx.device_status() == (N.OK, 0)   # cleared
+    assert np.isfinite(out).all()
+
+
+def test_load_layer_file(tmp_path):
+    bits = 2
+    ctx = N.Context(quant_bits=bits, num_layers=1, device=0)
+    lw = O.make_layer(21, bits=bits, distinct_experts=4)
+    p = tmp_path / "layer_00.bin"
+    lw.experts.tofile(p)
+    ctx.load_layer_file(0, str(p))
+    ctx.set_dense(0, lw.router, lw.shared_gate, lw.shared_up, lw.shared_down, lw.shared_gate_vec)
+    x, xd = make_x(4, N.DTYPE_BF16)
+    out, idx, w, lg = run_gpu(ctx, 0, 8, xd, N.DTYPE_BF16)
+    ref = O.block_forward(lw, 8, x, logits_override=lg)
+    assert rel_l2(out, ref["out"]) < 1e-4
+    (tmp_path / "short.bin").write_bytes(b"\0" * 1000)
+    with pytest.raises(N.NmoeError) as ei:
+        ctx.load_layer_file(0, str(tmp_path / "short.bin"))
+    assert ei.value.status == N.ESIZE
