@@ -169,6 +169,29 @@ int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int k, const v
  * NMOE_OK or NMOE_EDEVICE and the first recorded code in *code (may be NULL). */
 int nmoe_moe_device_status(nmoe_moe_ctx *ctx, int *code);
 
+/* ---- forward without any allocation ------------------------------------------ */
+
+/* No counterpart in the reference. The batch-1 block of nmoe_moe_forward for callers
+ * that cannot allocate device memory when they call: hosts whose device memory belongs
+ * to a preallocated pool they may not go around, code where cudaMalloc's implicit
+ * synchronisation is not allowed, embedders that never create an nmoe_moe_ctx.
+ * All weights are DEVICE pointers the caller owns, laid out as nmoe_moe_load_layer /
+ * nmoe_moe_set_dense take them on the host: `experts` is a layer_XX.bin image of
+ * num_experts expert blobs, `dense` holds the router/shared tensors. The call allocates
+ * nothing: its scratch (about 22 KB) is one array compiled into the library, held by
+ * every GPU that loads it until the process exits, and shared by all calls on a device.
+ * Limits: k in [1, 8] (the scratch holds 8 routed slots); larger k is rejected with
+ * NMOE_EINVAL. The first call on a device (the current one) looks up that array's device
+ * address; make that first call before any stream capture. Calls that overlap on the
+ * GPU (different streams, or different host threads) race on the shared scratch: order
+ * them. Routed ids >= num_experts contribute nothing. Message of a failed call:
+ * nmoe_moe_static_error(). */
+int nmoe_moe_forward_static(const void *experts, int num_experts, int quant_bits,
+                            const nmoe_moe_dense_weights *dense, int router_dtype, int shared_dtype,
+                            int k, const void *x, int x_dtype, const float *h_mid, float *out,
+                            uint32_t *idx_out, float *w_out, void *stream);
+const char *nmoe_moe_static_error(void);
+
 #ifdef __cplusplus
 }
 #endif

@@ -28,6 +28,7 @@ ABI_SYMBOLS = (
     "nmoe_moe_strerror", "nmoe_moe_create", "nmoe_moe_destroy", "nmoe_moe_create_error", "nmoe_moe_last_error",
     "nmoe_moe_load_layer", "nmoe_moe_load_layer_file", "nmoe_moe_set_dense",
     "nmoe_moe_forward", "nmoe_moe_route", "nmoe_moe_forward_batched", "nmoe_moe_device_status",
+    "nmoe_moe_forward_static", "nmoe_moe_static_error",
 )
 
 
@@ -99,6 +100,9 @@ def lib() -> C.CDLL:
     L.nmoe_moe_forward_batched.argtypes = [vp, i, i, i, vp, i, vp, vp, i, vp, vp, vp]
     L.nmoe_moe_device_status.restype = i
     L.nmoe_moe_device_status.argtypes = [vp, C.POINTER(i)]
+    L.nmoe_moe_forward_static.restype = i
+    L.nmoe_moe_forward_static.argtypes = [vp, i, i, C.POINTER(DenseWeights), i, i, i, vp, i, vp, vp, vp, vp, vp]
+    L.nmoe_moe_static_error.restype = C.c_char_p
     _lib = L
     return L
 
@@ -207,3 +211,19 @@ class Context:
         code = C.c_int(0)
         rc = self._L.nmoe_moe_device_status(self.h, C.byref(code))
         return rc, code.value
+
+
+def forward_static(experts, num_experts, quant_bits, dense, router_dtype, shared_dtype, k, x, out,
+                   x_dtype=DTYPE_BF16, h_mid=None, idx_out=None, w_out=None, stream=0):
+    """nmoe_moe_forward_static: batch-1 block over caller-owned DEVICE weights, allocating
+    nothing. `dense` maps router/shared_gate/shared_up/shared_down/shared_gate_vec to
+    dicts of device tensors/pointers {"weight", ["scales", "biases"]}."""
+    def t(d):
+        return Tensor(_ptr(d["weight"]), _ptr(d.get("scales")), _ptr(d.get("biases")))
+    dw = DenseWeights(t(dense["router"]), t(dense["shared_gate"]), t(dense["shared_up"]),
+                      t(dense["shared_down"]), t(dense["shared_gate_vec"]))
+    L = lib()
+    rc = L.nmoe_moe_forward_static(_ptr(experts), num_experts, quant_bits, C.byref(dw), router_dtype, shared_dtype,
+                                   k, _ptr(x), x_dtype, _ptr(h_mid), _ptr(out), _ptr(idx_out), _ptr(w_out), stream)
+    if rc != OK:
+        raise NmoeError(rc, L.nmoe_moe_static_error().decode())
