@@ -169,6 +169,15 @@ int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int k, const v
  * NMOE_OK or NMOE_EDEVICE and the first recorded code in *code (may be NULL). */
 int nmoe_moe_device_status(nmoe_moe_ctx *ctx, int *code);
 
+/* Diagnostics: copy and clear the single-launch decode kernel's per-CTA progress trail
+ * (n <= 1024 entries; entry c = highest phase 1..7 CTA c reached since the last read,
+ * 100 + phase where a bounded wait gave up). Synchronises the device. */
+int nmoe_moe_debug_trail(nmoe_moe_ctx *ctx, uint32_t *out, int n);
+/* Diagnostics: per-CTA phase timestamps (globaltimer ns, low 32 bits, [n_ctas][16]) of
+ * the last decode call, recorded when the context was created with NMOE_TIMELINE=1 in
+ * the environment. Synchronises the device. */
+int nmoe_moe_debug_timeline(nmoe_moe_ctx *ctx, uint32_t *out, int n_ctas);
+
 /* ---- forward without any allocation ------------------------------------------ */
 
 /* No counterpart in the reference. The batch-1 block of nmoe_moe_forward for callers

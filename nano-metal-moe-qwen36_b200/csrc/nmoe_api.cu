@@ -14,6 +14,7 @@
 #include "nmoe_ctx.cuh"
 #include "nmoe_decode.cuh"
 #include "nmoe_fused.cuh"
+#include "nmoe_pack.cuh"
 
 using namespace nmoe;
 
@@ -53,29 +54,24 @@ struct DeviceGuard {
 
 static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
-// Bytes of one dense matrix in the given dtype, and its (w, s, b) sub-offsets.
-static size_t dense_bytes(int rows, int cols, int dtype, size_t *w_b, size_t *s_b) {
-    if (dtype == NMOE_DTYPE_BF16) {
-        *w_b = (size_t)rows * cols * 2;
-        *s_b = 0;
-        return align256(*w_b);
-    }
-    *w_b = (size_t)rows * cols / 2;
-    *s_b = (size_t)rows * (cols / NMOE_GROUP) * 2;
-    return align256(*w_b) + 2 * align256(*s_b);
+// Dense arena of one layer, row-interleaved (nmoe_pack.cuh): router rows, shared
+// gate/up pairs, gate vector, shared down rows; each region 256-byte aligned.
+struct DenseArena {
+    size_t router, spairs, gvec, sdown, total;
+    uint32_t rrow, srow, sdrow;   // row bytes (router, shared gate/up, shared down)
+};
+static DenseArena dense_arena(int router_dtype, int shared_dtype) {
+    DenseArena a;
+    a.rrow = dense_row_bytes(router_dtype == NMOE_DTYPE_Q4, NMOE_HIDDEN);
+    a.srow = dense_row_bytes(shared_dtype == NMOE_DTYPE_Q4, NMOE_HIDDEN);
+    a.sdrow = dense_row_bytes(shared_dtype == NMOE_DTYPE_Q4, NMOE_INTER);
+    a.router = 0;
+    a.spairs = align256(a.router + (size_t)NMOE_NUM_EXPERTS * a.rrow);
+    a.gvec = align256(a.spairs + (size_t)NMOE_INTER * 2 * a.srow);
+    a.sdown = align256(a.gvec + a.srow);
+    a.total = align256(a.sdown + (size_t)NMOE_HIDDEN * a.sdrow);
+    return a;
 }
-
-struct DenseShape {
-    int rows, cols;
-    bool router;
-};
-static const DenseShape kDenseShapes[5] = {
-    {NMOE_NUM_EXPERTS, NMOE_HIDDEN, true},  // router
-    {NMOE_INTER, NMOE_HIDDEN, false},       // shared gate
-    {NMOE_INTER, NMOE_HIDDEN, false},       // shared up
-    {NMOE_HIDDEN, NMOE_INTER, false},       // shared down
-    {1, NMOE_HIDDEN, false},                // shared gate vector
-};
 
 // ------------------------------------------------------------- host helpers ----
 
@@ -166,13 +162,7 @@ extern "C" nmoe_moe_ctx *nmoe_moe_create(const nmoe_moe_config *cfg, int device,
     cudaGetDeviceProperties(&prop, device);
     ctx->num_sms = prop.multiProcessorCount;
 
-    // dense arena layout
-    size_t per_layer = 0;
-    for (int m = 0; m < 5; ++m) {
-        size_t wb, sb;
-        const int dt = kDenseShapes[m].router ? cfg->router_dtype : cfg->shared_dtype;
-        per_layer += dense_bytes(kDenseShapes[m].rows, kDenseShapes[m].cols, dt, &wb, &sb);
-    }
+    const size_t per_layer = dense_arena(cfg->router_dtype, cfg->shared_dtype).total;
     ctx->dense_layer_bytes = per_layer;
     ctx->expert_layer_bytes = (size_t)ctx->n_local * ctx->esz;
 
@@ -190,21 +180,24 @@ extern "C" nmoe_moe_ctx *nmoe_moe_create(const nmoe_moe_config *cfg, int device,
         return fail(ce, "cudaMalloc(dense)");
     if ((ce = cudaMemset(ctx->d_dense, 0, per_layer * cfg->num_layers)) != cudaSuccess)
         return fail(ce, "cudaMemset(dense)");
-    if ((ce = cudaMalloc(&ctx->d_ws, sizeof(DecodeScratch))) != cudaSuccess) return fail(ce, "cudaMalloc(ws)");
     if ((ce = cudaMalloc(&ctx->d_err, sizeof(int) * 4)) != cudaSuccess) return fail(ce, "cudaMalloc(err)");
     if ((ce = cudaMemset(ctx->d_err, 0, sizeof(int) * 4)) != cudaSuccess) return fail(ce, "cudaMemset(err)");
     ctx->loaded.assign(cfg->num_layers, 0);
     ctx->dense_set.assign(cfg->num_layers, 0);
-    if ((ce = nmoe_fused_init(ctx)) != cudaSuccess) return fail(ce, "fused decode init");
-    int bst = nmoe_batched_init(ctx);
+    int bst = nmoe_fused_init(ctx);
+    if (bst != NMOE_OK) {
+        snprintf(g_create_error, sizeof g_create_error, "decode kernel init: %s", ctx->last_error);
+        *st = bst;
+        nmoe_moe_destroy(ctx);
+        return nullptr;
+    }
+    bst = nmoe_batched_init(ctx);
     if (bst != NMOE_OK) {
         snprintf(g_create_error, sizeof g_create_error, "batched init: %s", ctx->last_error);
         *st = bst;
         nmoe_moe_destroy(ctx);
         return nullptr;
     }
-    const char *mode = getenv("NMOE_DECODE_KERNEL");
-    ctx->decode_mode = (mode && strcmp(mode, "staged") == 0) ? 1 : 0;
     *st = NMOE_OK;
     return ctx;
 }
@@ -216,12 +209,19 @@ extern "C" void nmoe_moe_destroy(nmoe_moe_ctx *ctx) {
     nmoe_fused_destroy(ctx);
     if (ctx->d_experts) cudaFree(ctx->d_experts);
     if (ctx->d_dense) cudaFree(ctx->d_dense);
-    if (ctx->d_ws) cudaFree(ctx->d_ws);
     if (ctx->d_err) cudaFree(ctx->d_err);
     delete ctx;
 }
 
 // ---------------------------------------------------------------- loading ----
+
+// Converter-layout blobs in device memory -> this layer's kernel-layout slot.
+static cudaError_t repack_layer(nmoe_moe_ctx *ctx, int layer, const uint8_t *stage) {
+    cudaError_t e = repack_experts(stage, ctx->d_experts + (size_t)layer * ctx->expert_layer_bytes, ctx->n_local,
+                                   ctx->cfg.quant_bits, 0);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(0);
+    return e;
+}
 
 extern "C" int nmoe_moe_load_layer(nmoe_moe_ctx *ctx, int layer, const void *layer_bin, size_t bytes) {
     if (ctx == nullptr) return NMOE_EINVAL;
@@ -237,8 +237,12 @@ extern "C" int nmoe_moe_load_layer(nmoe_moe_ctx *ctx, int layer, const void *lay
     }
     DeviceGuard guard(ctx->device);
     const uint8_t *src = static_cast<const uint8_t *>(layer_bin) + (size_t)ctx->expert_lo * ctx->esz;
-    NMOE_CUDA_TRY(ctx, cudaMemcpy(ctx->d_experts + (size_t)layer * ctx->expert_layer_bytes, src,
-                                  ctx->expert_layer_bytes, cudaMemcpyHostToDevice));
+    uint8_t *stage = nullptr;
+    NMOE_CUDA_TRY(ctx, cudaMalloc(&stage, ctx->expert_layer_bytes));
+    cudaError_t e = cudaMemcpy(stage, src, ctx->expert_layer_bytes, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = repack_layer(ctx, layer, stage);
+    cudaFree(stage);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "load_layer");
     ctx->loaded[layer] = 1;
     return NMOE_OK;
 }
@@ -267,7 +271,13 @@ extern "C" int nmoe_moe_load_layer_file(nmoe_moe_ctx *ctx, int layer, const char
     if (cudaMallocHost(&stage, chunk) != cudaSuccess) { fclose(f); nmoe_ctx_set_error(ctx, "pinned alloc"); return NMOE_ENOMEM; }
     int rc = NMOE_OK;
     fseek(f, (long)((size_t)ctx->expert_lo * ctx->esz), SEEK_SET);
-    uint8_t *dst = ctx->d_experts + (size_t)layer * ctx->expert_layer_bytes;
+    uint8_t *dst = nullptr;
+    if (cudaMalloc(&dst, ctx->expert_layer_bytes) != cudaSuccess) {
+        cudaFreeHost(stage);
+        fclose(f);
+        nmoe_ctx_set_error(ctx, "device staging alloc");
+        return NMOE_ENOMEM;
+    }
     for (size_t done = 0; done < ctx->expert_layer_bytes && rc == NMOE_OK;) {
         const size_t n = std::min(chunk, ctx->expert_layer_bytes - done);
         if (fread(stage, 1, n, f) != n) { nmoe_ctx_set_error(ctx, "short read of %s", path); rc = NMOE_EIO; break; }
@@ -277,25 +287,13 @@ extern "C" int nmoe_moe_load_layer_file(nmoe_moe_ctx *ctx, int layer, const char
     }
     cudaFreeHost(stage);
     fclose(f);
+    if (rc == NMOE_OK) {
+        cudaError_t e = repack_layer(ctx, layer, dst);
+        if (e != cudaSuccess) rc = cuda_fail(ctx, e, "repack");
+    }
+    cudaFree(dst);
     if (rc == NMOE_OK) ctx->loaded[layer] = 1;
     return rc;
-}
-
-LayerDev nmoe_ctx_layer(const nmoe_moe_ctx *ctx, int layer) {
-    LayerDev L;
-    L.experts = ctx->d_experts + (size_t)layer * ctx->expert_layer_bytes;
-    uint8_t *p = ctx->d_dense + (size_t)layer * ctx->dense_layer_bytes;
-    DenseDev *dst[5] = {&L.router, &L.sgate, &L.sup, &L.sdown, &L.gvec};
-    for (int m = 0; m < 5; ++m) {
-        size_t wb, sb;
-        const int dt = kDenseShapes[m].router ? ctx->cfg.router_dtype : ctx->cfg.shared_dtype;
-        const size_t tot = dense_bytes(kDenseShapes[m].rows, kDenseShapes[m].cols, dt, &wb, &sb);
-        dst[m]->w = p;
-        dst[m]->s = dt == NMOE_DTYPE_Q4 ? reinterpret_cast<const uint16_t *>(p + align256(wb)) : nullptr;
-        dst[m]->b = dt == NMOE_DTYPE_Q4 ? reinterpret_cast<const uint16_t *>(p + align256(wb) + align256(sb)) : nullptr;
-        p += tot;
-    }
-    return L;
 }
 
 extern "C" int nmoe_moe_set_dense(nmoe_moe_ctx *ctx, int layer, const nmoe_moe_dense_weights *w) {
@@ -304,24 +302,48 @@ extern "C" int nmoe_moe_set_dense(nmoe_moe_ctx *ctx, int layer, const nmoe_moe_d
         nmoe_ctx_set_error(ctx, "set_dense: bad layer %d or null weights", layer);
         return NMOE_EINVAL;
     }
-    DeviceGuard guard(ctx->device);
+    const bool rq4 = ctx->cfg.router_dtype == NMOE_DTYPE_Q4, sq4 = ctx->cfg.shared_dtype == NMOE_DTYPE_Q4;
     const nmoe_tensor *src[5] = {&w->router, &w->shared_gate, &w->shared_up, &w->shared_down, &w->shared_gate_vec};
-    uint8_t *p = ctx->d_dense + (size_t)layer * ctx->dense_layer_bytes;
     for (int m = 0; m < 5; ++m) {
-        size_t wb, sb;
-        const int dt = kDenseShapes[m].router ? ctx->cfg.router_dtype : ctx->cfg.shared_dtype;
-        const size_t tot = dense_bytes(kDenseShapes[m].rows, kDenseShapes[m].cols, dt, &wb, &sb);
-        if (src[m]->weight == nullptr || (dt == NMOE_DTYPE_Q4 && (src[m]->scales == nullptr || src[m]->biases == nullptr))) {
+        const bool q4 = m == 0 ? rq4 : sq4;
+        if (src[m]->weight == nullptr || (q4 && (src[m]->scales == nullptr || src[m]->biases == nullptr))) {
             nmoe_ctx_set_error(ctx, "set_dense: tensor %d missing weight/scales/biases", m);
             return NMOE_EINVAL;
         }
-        NMOE_CUDA_TRY(ctx, cudaMemcpy(p, src[m]->weight, wb, cudaMemcpyHostToDevice));
-        if (dt == NMOE_DTYPE_Q4) {
-            NMOE_CUDA_TRY(ctx, cudaMemcpy(p + align256(wb), src[m]->scales, sb, cudaMemcpyHostToDevice));
-            NMOE_CUDA_TRY(ctx, cudaMemcpy(p + align256(wb) + align256(sb), src[m]->biases, sb, cudaMemcpyHostToDevice));
-        }
-        p += tot;
     }
+    const DenseArena A = dense_arena(ctx->cfg.router_dtype, ctx->cfg.shared_dtype);
+    std::vector<uint8_t> h(A.total, 0);
+    // one row of a [rows][cols] matrix as [w | s | b] (q4) or [w] (bf16)
+    auto put_row = [&](uint8_t *dst, const nmoe_tensor *t, bool q4, int row, int cols) {
+        if (!q4) {
+            memcpy(dst, static_cast<const uint8_t *>(t->weight) + (size_t)row * cols * 2, (size_t)cols * 2);
+            return;
+        }
+        const size_t wb = cols / 2, sb = (cols / 64) * 2;
+        memcpy(dst, static_cast<const uint8_t *>(t->weight) + row * wb, wb);
+        memcpy(dst + wb, static_cast<const uint8_t *>(t->scales) + row * sb, sb);
+        memcpy(dst + wb + sb, static_cast<const uint8_t *>(t->biases) + row * sb, sb);
+    };
+    for (int r = 0; r < NMOE_NUM_EXPERTS; ++r) put_row(&h[A.router + (size_t)r * A.rrow], src[0], rq4, r, NMOE_HIDDEN);
+    for (int r = 0; r < NMOE_INTER; ++r) {
+        uint8_t *pr = &h[A.spairs + (size_t)r * 2 * A.srow];
+        if (!sq4) {
+            put_row(pr, src[1], false, r, NMOE_HIDDEN);
+            put_row(pr + A.srow, src[2], false, r, NMOE_HIDDEN);
+        } else {   // [gate.w | up.w | gate.s | gate.b | up.s | up.b]
+            memcpy(pr, static_cast<const uint8_t *>(src[1]->weight) + (size_t)r * 1024, 1024);
+            memcpy(pr + 1024, static_cast<const uint8_t *>(src[2]->weight) + (size_t)r * 1024, 1024);
+            memcpy(pr + 2048, static_cast<const uint8_t *>(src[1]->scales) + (size_t)r * 64, 64);
+            memcpy(pr + 2112, static_cast<const uint8_t *>(src[1]->biases) + (size_t)r * 64, 64);
+            memcpy(pr + 2176, static_cast<const uint8_t *>(src[2]->scales) + (size_t)r * 64, 64);
+            memcpy(pr + 2240, static_cast<const uint8_t *>(src[2]->biases) + (size_t)r * 64, 64);
+        }
+    }
+    put_row(&h[A.gvec], src[4], sq4, 0, NMOE_HIDDEN);
+    for (int r = 0; r < NMOE_HIDDEN; ++r) put_row(&h[A.sdown + (size_t)r * A.sdrow], src[3], sq4, r, NMOE_INTER);
+    DeviceGuard guard(ctx->device);
+    NMOE_CUDA_TRY(ctx, cudaMemcpy(ctx->d_dense + (size_t)layer * ctx->dense_layer_bytes, h.data(), A.total,
+                                  cudaMemcpyHostToDevice));
     ctx->dense_set[layer] = 1;
     return NMOE_OK;
 }
@@ -349,22 +371,26 @@ int nmoe_ctx_check_call(nmoe_moe_ctx *ctx, int layer, int k, int x_dtype) {
     return NMOE_OK;
 }
 
-static DecodeArgs make_args(nmoe_moe_ctx *ctx, int layer, int k, const void *x, int x_dtype, const float *h_mid,
-                            float *out, uint32_t *idx_out, float *w_out) {
-    DecodeArgs a;
-    a.L = nmoe_ctx_layer(ctx, layer);
-    a.bits = ctx->cfg.quant_bits;
-    a.router_q4 = ctx->cfg.router_dtype == NMOE_DTYPE_Q4;
-    a.shared_q4 = ctx->cfg.shared_dtype == NMOE_DTYPE_Q4;
-    a.num_experts = ctx->cfg.num_experts;
-    a.k = k;
+static FusedCall make_call(nmoe_moe_ctx *ctx, int layer, int k, const void *x, int x_dtype, const float *h_mid,
+                           float *out, uint32_t *idx_out, float *w_out, float *logits_out, int route_only) {
+    const DenseArena A = dense_arena(ctx->cfg.router_dtype, ctx->cfg.shared_dtype);
+    const uint8_t *d = ctx->d_dense + (size_t)layer * ctx->dense_layer_bytes;
+    FusedCall a;
+    a.experts = ctx->d_experts + (size_t)layer * ctx->expert_layer_bytes;
+    a.router = d + A.router;
+    a.spairs = d + A.spairs;
+    a.gvec = d + A.gvec;
+    a.sdown = d + A.sdown;
     a.x = x;
     a.x_f32 = x_dtype == NMOE_DTYPE_F32;
     a.h_mid = h_mid;
     a.out = out;
     a.idx_out = idx_out;
     a.w_out = w_out;
-    a.ws = ctx->d_ws;
+    a.logits_out = logits_out;
+    a.k = k;
+    a.num_experts = ctx->cfg.num_experts;
+    a.route_only = route_only;
     a.err = ctx->d_err;
     return a;
 }
@@ -374,14 +400,14 @@ extern "C" int nmoe_moe_forward(nmoe_moe_ctx *ctx, int layer, int k, const void 
     int rc = nmoe_ctx_check_call(ctx, layer, k, x_dtype);
     if (rc != NMOE_OK) return rc;
     if (x == nullptr || out == nullptr) { nmoe_ctx_set_error(ctx, "x and out are required"); return NMOE_EINVAL; }
+    if (reinterpret_cast<uintptr_t>(x) % 16 != 0) { nmoe_ctx_set_error(ctx, "x must be 16-byte aligned"); return NMOE_EINVAL; }
     if (ctx->cfg.world_size > 1) {
         nmoe_ctx_set_error(ctx, "batch-1 decode runs on replicas (world_size 1); use forward_batched for EP");
         return NMOE_EINVAL;
     }
     DeviceGuard guard(ctx->device);
-    DecodeArgs a = make_args(ctx, layer, k, x, x_dtype, h_mid, out, idx_out, w_out);
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    cudaError_t e = ctx->decode_mode == 1 ? launch_decode_staged(a, st) : nmoe_fused_launch(ctx, a, st);
+    cudaError_t e = nmoe_fused_launch(ctx, make_call(ctx, layer, k, x, x_dtype, h_mid, out, idx_out, w_out, nullptr, 0),
+                                      static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(ctx, e, "decode launch");
     return NMOE_OK;
 }
@@ -391,9 +417,12 @@ extern "C" int nmoe_moe_route(nmoe_moe_ctx *ctx, int layer, int k, const void *x
     int rc = nmoe_ctx_check_call(ctx, layer, k, x_dtype);
     if (rc != NMOE_OK) return rc;
     if (x == nullptr) { nmoe_ctx_set_error(ctx, "x is required"); return NMOE_EINVAL; }
+    if (reinterpret_cast<uintptr_t>(x) % 16 != 0) { nmoe_ctx_set_error(ctx, "x must be 16-byte aligned"); return NMOE_EINVAL; }
     DeviceGuard guard(ctx->device);
-    DecodeArgs a = make_args(ctx, layer, k, x, x_dtype, nullptr, nullptr, idx_out, w_out);
-    cudaError_t e = launch_route(a, static_cast<cudaStream_t>(stream), logits_out);
+    // the same kernel, stopped after routing: the same fp32 logits as nmoe_moe_forward
+    cudaError_t e = nmoe_fused_launch(ctx, make_call(ctx, layer, k, x, x_dtype, nullptr, nullptr, idx_out, w_out,
+                                                     logits_out, 1),
+                                      static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(ctx, e, "route launch");
     return NMOE_OK;
 }

@@ -23,10 +23,8 @@ struct nmoe_moe_ctx {
     size_t dense_layer_bytes = 0;
     uint8_t *d_experts = nullptr;   // [num_layers][n_local * esz]
     uint8_t *d_dense = nullptr;     // [num_layers][dense_layer_bytes]
-    nmoe::DecodeScratch *d_ws = nullptr;
     int *d_err = nullptr;           // device error word (+3 spare ints)
     std::vector<char> loaded, dense_set;
-    int decode_mode = 0;            // 0 fused (default), 1 staged (NMOE_DECODE_KERNEL=staged)
     nmoe::FusedState *fused = nullptr;
     nmoe::BatchedState *batched = nullptr;
     nmoe::EpState *ep = nullptr;
@@ -34,5 +32,4 @@ struct nmoe_moe_ctx {
 };
 
 void nmoe_ctx_set_error(nmoe_moe_ctx *ctx, const char *fmt, ...);
-nmoe::LayerDev nmoe_ctx_layer(const nmoe_moe_ctx *ctx, int layer);
 int nmoe_ctx_check_call(nmoe_moe_ctx *ctx, int layer, int k, int x_dtype);

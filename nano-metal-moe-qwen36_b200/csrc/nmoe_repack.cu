@@ -1,0 +1,45 @@
+// nmoe_repack.cu -- converter layout (EXPERT_LAYOUT, scripts/convert_qwen36.py:38-64)
+// -> the decode kernel's band layout (nmoe_pack.cuh). One thread per 32-bit word of the
+// destination; a pure permutation (same byte count).
+#include "nmoe_fused.cuh"
+#include "nmoe_pack.cuh"
+
+namespace nmoe {
+
+__global__ void k_repack(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, int n_experts, int bits) {
+    const PackGeo pg = pack_geo(bits);
+    const ExpertOffsets eo = expert_offsets(bits);
+    const size_t words = (size_t)n_experts * pg.esz / 4;
+    for (size_t wi = blockIdx.x * (size_t)blockDim.x + threadIdx.x; wi < words; wi += (size_t)gridDim.x * blockDim.x) {
+        const size_t e = wi * 4 / pg.esz;
+        const uint32_t d = (uint32_t)(wi * 4 - e * pg.esz);
+        uint32_t s;   // source byte offset within the blob
+        if (d < pg.gu_bytes) {
+            const uint32_t bp = d / pg.bp, r = d % pg.bp;
+            if (r < 2 * pg.tile_band_gu) {   // 16 gate rows then 16 up rows, row-major
+                const uint32_t mat = r / pg.tile_band_gu, q = r % pg.tile_band_gu;
+                s = (mat ? eo.uw : eo.gw) + 16 * bp * pg.wgu * 4 + q;
+            } else {                          // gs, gb, us, ub: [16][32] bf16 each
+                const uint32_t r2 = r - 2 * pg.tile_band_gu, which = r2 / 1024, q = r2 % 1024;
+                const uint32_t comp[4] = {eo.gs, eo.gb, eo.us, eo.ub};
+                s = comp[which] + 16 * bp * 64 + q;
+            }
+        } else {
+            const uint32_t d2 = d - pg.gu_bytes, b = d2 / pg.db, r = d2 % pg.db;
+            if (r < pg.tile_band_d) {
+                s = eo.dw + 16 * b * pg.wd * 4 + r;
+            } else {
+                const uint32_t r2 = r - pg.tile_band_d, which = r2 / 256, q = r2 % 256;
+                s = (which ? eo.db : eo.ds) + 16 * b * 16 + q;
+            }
+        }
+        reinterpret_cast<uint32_t *>(dst)[wi] = *reinterpret_cast<const uint32_t *>(src + e * pg.esz + s);
+    }
+}
+
+cudaError_t repack_experts(const uint8_t *src, uint8_t *dst, int n_experts, int bits, cudaStream_t st) {
+    k_repack<<<1184, 256, 0, st>>>(src, dst, n_experts, bits);
+    return cudaGetLastError();
+}
+
+}  // namespace nmoe

@@ -28,7 +28,7 @@ ABI_SYMBOLS = (
     "nmoe_moe_strerror", "nmoe_moe_create", "nmoe_moe_destroy", "nmoe_moe_create_error", "nmoe_moe_last_error",
     "nmoe_moe_load_layer", "nmoe_moe_load_layer_file", "nmoe_moe_set_dense",
     "nmoe_moe_forward", "nmoe_moe_route", "nmoe_moe_forward_batched", "nmoe_moe_device_status",
-    "nmoe_moe_forward_static", "nmoe_moe_static_error",
+    "nmoe_moe_forward_static", "nmoe_moe_static_error", "nmoe_moe_debug_trail", "nmoe_moe_debug_timeline",
 )
 
 
@@ -103,6 +103,10 @@ def lib() -> C.CDLL:
     L.nmoe_moe_forward_static.restype = i
     L.nmoe_moe_forward_static.argtypes = [vp, i, i, C.POINTER(DenseWeights), i, i, i, vp, i, vp, vp, vp, vp, vp]
     L.nmoe_moe_static_error.restype = C.c_char_p
+    L.nmoe_moe_debug_trail.restype = i
+    L.nmoe_moe_debug_trail.argtypes = [vp, vp, i]
+    L.nmoe_moe_debug_timeline.restype = i
+    L.nmoe_moe_debug_timeline.argtypes = [vp, vp, i]
     _lib = L
     return L
 
@@ -206,6 +210,16 @@ class Context:
                         idx_out=None, w_out=None, stream=0):
         self._check(self._L.nmoe_moe_forward_batched(self.h, layer, T, k, _ptr(x), x_dtype, _ptr(h_mid), _ptr(out),
                                                      out_dtype, _ptr(idx_out), _ptr(w_out), stream))
+
+    def debug_trail(self, n=1024):
+        out = np.zeros(n, np.uint32)
+        self._check(self._L.nmoe_moe_debug_trail(self.h, out.ctypes.data, n))
+        return out
+
+    def debug_timeline(self, n_ctas=148):
+        out = np.zeros((n_ctas, 16), np.uint32)
+        self._check(self._L.nmoe_moe_debug_timeline(self.h, out.ctypes.data, n_ctas))
+        return out
 
     def device_status(self):
         code = C.c_int(0)

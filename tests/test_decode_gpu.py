@@ -16,6 +16,11 @@ torch = pytest.importorskip("torch")
 
 pytestmark = pytest.mark.gpu
 
+# Output tolerance (relative L2) of the default path, whose routed-expert dot products
+# run in half2 with fp32 flushes (~3e-4 typical); the requirement is 1e-2. The fp32
+# expert path (NMOE_EXPERT_FP32=1) is held to 1e-4 in test_fp32_expert_path.
+OUT_TOL = 2e-3
+
 CONFIGS = {
     # name: (bits, router dtype, shared dtype, x dtype)
     "cfg0_q4_bf16": (4, N.DTYPE_BF16, N.DTYPE_BF16, N.DTYPE_BF16),
@@ -70,15 +75,16 @@ def test_block_matches_oracle(name, k):
             x, xd = make_x(1000 * layer + 10 * k + trial, x_dtype)
             out, idx, w, lg = run_gpu(ctx, layer, k, xd, x_dtype)
             ref = O.block_forward(layers[layer], k, x, logits_override=lg)
-            # logits: fp32 accumulation order differs only
-            assert rel_l2(lg, ref["logits"]) < 1e-5
+            # logits: fp32 arithmetic differs in order (and, on q4 rows, in the conversion-free
+            # dequant, about 1e-5 relative); routing is checked on these logits below
+            assert rel_l2(lg, ref["logits"]) < 5e-5
             # routing on the GPU's logits is bit-exact with the reference rule
             ridx, rw = O.route_reference(lg, k)
             np.testing.assert_array_equal(idx[:k], ridx)
             np.testing.assert_array_equal(idx[k:], 0)
             np.testing.assert_allclose(w[:k], rw, rtol=2e-6, atol=1e-7)
             np.testing.assert_array_equal(w[k:], 0)
-            assert rel_l2(out, ref["out"]) < 1e-4, rel_l2(out, ref["out"])
+            assert rel_l2(out, ref["out"]) < OUT_TOL, rel_l2(out, ref["out"])
             # the oracle routing on its own logits agrees unless the k-th/(k+1)-th gap is a near tie
             own = O.block_forward(layers[layer], k, x)
             if not np.array_equal(own["idx"][:k], idx[:k]):
@@ -94,7 +100,7 @@ def test_residual_h_mid(name):
     hm = np.random.default_rng(6).standard_normal(2048, dtype=np.float32)
     out, _, _, lg = run_gpu(ctx, 0, 8, xd, x_dtype, torch.from_numpy(hm).cuda())
     ref = O.block_forward(layers[0], 8, x, h_mid=hm, logits_override=lg)
-    assert rel_l2(out, ref["out"]) < 1e-5
+    assert rel_l2(out, ref["out"]) < OUT_TOL
 
 
 def test_tie_goes_to_lower_expert_id():
@@ -186,8 +192,59 @@ def test_load_layer_file(tmp_path):
     x, xd = make_x(4, N.DTYPE_BF16)
     out, idx, w, lg = run_gpu(ctx, 0, 8, xd, N.DTYPE_BF16)
     ref = O.block_forward(lw, 8, x, logits_override=lg)
-    assert rel_l2(out, ref["out"]) < 1e-4
+    assert rel_l2(out, ref["out"]) < OUT_TOL
     (tmp_path / "short.bin").write_bytes(b"\0" * 1000)
     with pytest.raises(N.NmoeError) as ei:
         ctx.load_layer_file(0, str(tmp_path / "short.bin"))
     assert ei.value.status == N.ESIZE
+
+
+def test_repeated_calls_are_identical_and_counters_reset():
+    ctx, layers = setup("cfg0_q4_bf16")
+    x, xd = make_x(31, N.DTYPE_BF16)
+    hm = torch.randn(2048, device="cuda")
+    outs = [run_gpu(ctx, 0, 8, xd, N.DTYPE_BF16, hm)[0] for _ in range(4)]
+    for o in outs[1:]:
+        np.testing.assert_array_equal(outs[0], o)
+    assert ctx.device_status() == (N.OK, 0)
+    trail = ctx.debug_trail(1024)
+    assert (trail[:148] == 7).all() or (trail[trail > 0] == 7).all()
+
+
+def test_bounded_wait_timeout_reports_and_recovers(monkeypatch):
+    """A zero wait budget makes the kernel's cross-CTA waits expire: the call returns, the
+    host reads NMOE_ETIMEOUT from the device error word, and the device stays usable."""
+    lw = O.make_layer(77, bits=4, distinct_experts=8)
+    monkeypatch.setenv("NMOE_WAIT_TIMEOUT_MS", "0")
+    ct = N.Context(quant_bits=4, num_layers=1, device=0)
+    monkeypatch.delenv("NMOE_WAIT_TIMEOUT_MS")
+    upload(ct, 0, lw)
+    x, xd = make_x(8, N.DTYPE_BF16)
+    out = torch.zeros(2048, dtype=torch.float32, device="cuda")
+    ct.forward(0, 8, xd, out)
+    rc, code = ct.device_status()
+    assert rc == N.ETIMEOUT and code == 2
+    ct.close()
+    cn = N.Context(quant_bits=4, num_layers=1, device=0)
+    upload(cn, 0, lw)
+    o, idx, w, lg = run_gpu(cn, 0, 8, xd, N.DTYPE_BF16)
+    ref = O.block_forward(lw, 8, x, logits_override=lg)
+    assert rel_l2(o, ref["out"]) < OUT_TOL
+    assert cn.device_status() == (N.OK, 0)
+
+
+@pytest.mark.parametrize("name", ["cfg0_q4_bf16", "ref_q4_q4_f32", "cfg1_q2_bf16"])
+def test_fp32_expert_path(monkeypatch, name):
+    """NMOE_EXPERT_FP32=1 selects fp32 routed-expert dot products: 1e-4 bar."""
+    bits, rdt, sdt, x_dtype = CONFIGS[name]
+    lw = O.make_layer(66, bits=bits, router_dtype=rdt, shared_dtype=sdt, distinct_experts=12)
+    monkeypatch.setenv("NMOE_EXPERT_FP32", "1")
+    ctx = N.Context(quant_bits=bits, num_layers=1, router_dtype=rdt, shared_dtype=sdt, device=0)
+    monkeypatch.delenv("NMOE_EXPERT_FP32")
+    upload(ctx, 0, lw)
+    for t in range(3):
+        x, xd = make_x(500 + t, x_dtype)
+        out, idx, w, lg = run_gpu(ctx, 0, 8, xd, x_dtype)
+        ref = O.block_forward(lw, 8, x, logits_override=lg)
+        np.testing.assert_array_equal(idx, ref["idx"])
+        assert rel_l2(out, ref["out"]) < 1e-4, rel_l2(out, ref["out"])

@@ -47,8 +47,10 @@ def test_static_forward_matches_context_forward(bits, rdt, xdt):
         N.forward_static(experts, 256, bits, dense, rdt, rdt, k, xd, o2, x_dtype=xdt, h_mid=hm, idx_out=i2, w_out=w2)
         torch.cuda.synchronize()
         np.testing.assert_array_equal(i1.cpu().numpy(), i2.cpu().numpy())
-        np.testing.assert_allclose(w1.cpu().numpy(), w2.cpu().numpy(), rtol=2e-6, atol=1e-7)
-        assert rel_l2(o2.cpu().numpy(), o1.cpu().numpy()) < 1e-4
+        # the two paths compute the router logits in different fp32 orders (~1e-5 relative)
+        np.testing.assert_allclose(w1.cpu().numpy(), w2.cpu().numpy(), rtol=1e-4, atol=1e-6)
+        # the context path's routed-expert dots run in half2 (see test_decode_gpu.OUT_TOL)
+        assert rel_l2(o2.cpu().numpy(), o1.cpu().numpy()) < 2e-3
 
 
 def test_static_forward_rejects_k_beyond_scratch():
