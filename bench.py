@@ -227,7 +227,8 @@ def run_ours(args, rank, world, local_rank):
     bits, k, rdt, sdt = 4, 8, N.DTYPE_BF16, N.DTYPE_BF16
     L = args.layers
     layers, xs_h = build_workload(L, bits, k, rdt, sdt, pool=args.pool, seed=args.seed + rank)
-    ctx = N.Context(quant_bits=bits, num_layers=L, router_dtype=rdt, shared_dtype=sdt, device=dev)
+    flags = N.FLAG_PREFETCH_NEXT_LAYER if args.prefetch else 0
+    ctx = N.Context(quant_bits=bits, num_layers=L, router_dtype=rdt, shared_dtype=sdt, device=dev, flags=flags)
     for l, lw in enumerate(layers):
         ctx.load_layer(l, lw.experts)
         ctx.set_dense(l, lw.router, lw.shared_gate, lw.shared_up, lw.shared_down, lw.shared_gate_vec)
@@ -326,7 +327,7 @@ def run_ours(args, rank, world, local_rank):
         abytes = algorithmic_bytes(bits, k, rdt, sdt)
         pk, pk_kind = peaks()
         achieved = abytes / per_launch_s / 1e9
-        launches_per_call = 4 if os.environ.get("NMOE_DECODE_KERNEL") == "staged" else 1
+        launches_per_call = 1   # one persistent kernel per layer call
         cpu = None
         if world == 1:
             v, cores, n, el = cpu_baseline_sample(cpu_layers, xs_h, k, args.cpu_seconds)
@@ -343,10 +344,11 @@ def run_ours(args, rank, world, local_rank):
                        "layers": L, "k": k, "step": f"{L} layer calls (one token through {L} MoE blocks)",
                        "l2": "inputs larger than L2 (a step touches ~860 MB of weights)",
                        "parallelism": "replicas only" if world > 1 else "single GPU",
-                       "timing": "CUDA graph of one step, CUDA events, max over ranks"},
+                       "timing": "CUDA graph of one step, CUDA events, max over ranks",
+                       "next_layer_prefetch": bool(args.prefetch)},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk, "unit": "GB/s", "frac": achieved / pk,
                          "peak_kind": pk_kind, "algorithmic_bytes_per_launch": abytes,
-                         "traffic": profiled_traffic("decode_cfg0")},
+                         "traffic": profiled_traffic("decode_fused_cfg0")},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": L * HIDDEN * 2,
                     "d2h_bytes_per_step": L * HIDDEN * 4},
@@ -368,6 +370,8 @@ def main():
     ap.add_argument("--pool", type=int, default=32, help="distinct expert packs generated on the host")
     ap.add_argument("--seed", type=int, default=2026)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--prefetch", action="store_true",
+                    help="let each layer call prefetch the next layer's router/shared weights to L2")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))

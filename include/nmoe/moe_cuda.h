@@ -70,7 +70,17 @@ typedef struct nmoe_moe_config {
     int world_size;    /* expert-parallel ranks (1 = single GPU)                             */
     int rank;          /* this process's rank, 0..world_size-1                               */
     const void *nccl_unique_id; /* 128-byte ncclUniqueId shared by all ranks (world_size>1)  */
+    int flags;         /* NMOE_FLAG_* bits, 0 for the defaults                                */
 } nmoe_moe_config;
+
+/* Opt-in behaviour (nmoe_moe_config.flags). */
+/* Layers are called in order 0, 1, ... (a decode step): each batch-1 call also pulls the
+ * next layer's router and shared-expert weights into L2 during its tail, so the next call
+ * starts from L2. Harmless but useless for other call orders. */
+#define NMOE_FLAG_PREFETCH_NEXT_LAYER 1
+/* Routed-expert dot products in fp32 (about 1e-6 relative) instead of the default half2
+ * products with fp32 flushes (about 3e-4 relative, twice the throughput). */
+#define NMOE_FLAG_EXPERT_FP32 2
 
 /* A matrix given to nmoe_moe_set_dense: bf16 uses `weight` only ([rows][cols] u16);
  * q4 uses weight ([rows][cols/8] u32), scales and biases ([rows][cols/64] bf16), the

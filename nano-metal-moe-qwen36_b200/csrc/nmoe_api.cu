@@ -198,6 +198,8 @@ extern "C" nmoe_moe_ctx *nmoe_moe_create(const nmoe_moe_config *cfg, int device,
         nmoe_moe_destroy(ctx);
         return nullptr;
     }
+    ctx->prefetch_next = (cfg->flags & NMOE_FLAG_PREFETCH_NEXT_LAYER) != 0;
+    if (const char *pf = getenv("NMOE_PREFETCH_NEXT")) ctx->prefetch_next = atoi(pf) != 0;
     *st = NMOE_OK;
     return ctx;
 }
@@ -392,6 +394,13 @@ static FusedCall make_call(nmoe_moe_ctx *ctx, int layer, int k, const void *x, i
     a.num_experts = ctx->cfg.num_experts;
     a.route_only = route_only;
     a.err = ctx->d_err;
+    a.next_dense = nullptr;
+    a.next_dense_bytes = 0;
+    if (ctx->prefetch_next && !route_only) {
+        const int nl = (layer + 1) % ctx->cfg.num_layers;
+        a.next_dense = ctx->d_dense + (size_t)nl * ctx->dense_layer_bytes;
+        a.next_dense_bytes = (uint32_t)ctx->dense_layer_bytes;
+    }
     return a;
 }
 

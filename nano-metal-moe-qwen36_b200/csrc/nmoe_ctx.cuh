@@ -25,6 +25,7 @@ struct nmoe_moe_ctx {
     uint8_t *d_dense = nullptr;     // [num_layers][dense_layer_bytes]
     int *d_err = nullptr;           // device error word (+3 spare ints)
     std::vector<char> loaded, dense_set;
+    int prefetch_next = 0;          // NMOE_PREFETCH_NEXT=1: prefetch layer+1's dense weights to L2
     nmoe::FusedState *fused = nullptr;
     nmoe::BatchedState *batched = nullptr;
     nmoe::EpState *ep = nullptr;

@@ -56,7 +56,8 @@ struct FusedSync {
     uint64_t shared_act[kInter];
     uint64_t score;
     uint64_t pad2[15];
-    uint64_t act[kMaxK * kInter];
+    float act[kMaxK * kInter];       // plain; readiness is per unit in uflag
+    uint32_t uflag[32 * kMaxK];      // tag of the launch whose unit u act rows are written
     uint32_t diag[1024];        // per CTA: highest phase reached; 100+phase where a wait gave up
     uint32_t tl[1024][16];      // per CTA phase timestamps (globaltimer low 32 bits)
 };
@@ -72,6 +73,8 @@ struct FusedLayout {
 struct FusedParams {
     const uint8_t *experts;   // repacked expert blobs of this layer
     const uint8_t *router, *spairs, *gvec, *sdown;   // repacked dense regions
+    const uint8_t *next_dense;   // dense arena to prefetch into L2 during the tail, or null
+    uint32_t next_dense_bytes;
     const void *x;
     int x_f32;
     const float *h_mid;
@@ -95,8 +98,8 @@ struct Ctl {
     float w[kMaxK];
     int valid[kMaxK];
     float score;
-    float cval[kExperts];
-    int cidx[kExperts];
+    __align__(16) float cval[kExperts + 4];
+    __align__(16) int cidx[kExperts + 4];
     float sel_v[kMaxK];
 };
 
@@ -333,6 +336,62 @@ __device__ __forceinline__ __half2 pair_entry(const float *vpad, int e, int E) {
         atomicMax(&P.sy->diag[c & 1023], 100u + (v));         \
     } while (0)
 
+// Top-k of the 256 logits held 8 per lane (lane l: experts 8l..8l+7), one warp.
+// Rule of nmoe_cpu_topk (src/math.m:95-132) on the logits: descending, lower expert id
+// first on ties. Writes S->idx[0..k) and S->sel_v[0..k) (the selected logits).
+// Candidates are the logits >= min over 8 groups (4 lanes, 32 logits) of the group
+// maximum -- at least 8 logits qualify, so the top-k (k <= 8) are among them -- ranked
+// against each other.
+__device__ __forceinline__ void warp_topk(const float *v, int k, Ctl *S, int lane) {
+    float m = v[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) m = fmaxf(m, v[i]);
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    float thr = m;
+    thr = fminf(thr, __shfl_xor_sync(0xffffffffu, thr, 4));
+    thr = fminf(thr, __shfl_xor_sync(0xffffffffu, thr, 8));
+    thr = fminf(thr, __shfl_xor_sync(0xffffffffu, thr, 16));
+    // candidate positions from 8 ballots (value slot j major, lane minor)
+    const uint32_t lt = (1u << lane) - 1u;
+    int base = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const bool cand = !(v[j] < thr);
+        const uint32_t b = __ballot_sync(0xffffffffu, cand);
+        if (cand) {
+            S->cval[base + __popc(b & lt)] = v[j];
+            S->cidx[base + __popc(b & lt)] = 8 * lane + j;
+        }
+        base += __popc(b);
+    }
+    const int nc = base;
+    const int ncp = (nc + 3) & ~3;   // pad to a multiple of 4 with entries that never win
+    if (lane < ncp - nc) {
+        S->cval[nc + lane] = -INFINITY;
+        S->cidx[nc + lane] = 1 << 20;
+    }
+    __syncwarp();
+    for (int q = lane; q < nc; q += 32) {
+        const float vi = S->cval[q];
+        const int ii = S->cidx[q];
+        int rank = 0;
+        for (int j = 0; j < ncp; j += 4) {
+            const float4 u = *reinterpret_cast<const float4 *>(&S->cval[j]);
+            const int4 ui = *reinterpret_cast<const int4 *>(&S->cidx[j]);
+            rank += (u.x > vi) | ((u.x == vi) & (ui.x < ii));
+            rank += (u.y > vi) | ((u.y == vi) & (ui.y < ii));
+            rank += (u.z > vi) | ((u.z == vi) & (ui.z < ii));
+            rank += (u.w > vi) | ((u.w == vi) & (ui.w < ii));
+        }
+        if (rank < k) {
+            S->idx[rank] = (uint32_t)ii;
+            S->sel_v[rank] = vi;
+        }
+    }
+    __syncwarp();
+}
+
 template <int kBits, bool kRQ4, bool kSQ4, bool kHalf>
 __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedParams P) {
     extern __shared__ __align__(1024) uint8_t sm[];
@@ -405,6 +464,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
                          &bars[kBarSDown], pol);
     };
     if (tid == 0 && P.shared_early && nR == 0) issue_shared();
+    // The routed down bands are only needed after the act exchange: they go out once this
+    // CTA's first gate/up unit has landed, so that the gate/up bytes are not interleaved
+    // with them in HBM.
+    auto issue_bands = [&]() {
+        const uint64_t pol = policy_evict_first();
+        for (int i = 0; i < nB; ++i) {
+            const int band = band0 + i * G;
+            for (int s = 0; s < k; ++s)
+                if (S->valid[s])
+                    bulk_g2s(sm + Y.bands + (i * Y.kmax + s) * pg.db,
+                             P.experts + (size_t)S->idx[s] * pg.esz + pg.gu_bytes + (size_t)band * pg.db, pg.db,
+                             &bars[kBarBand0 + i], pol);
+        }
+    };
 
     // ---- 1. x: fp32 padded + per-32-column parity sums + per-64-column group sums -----
     if (!mbar_wait_warp(&bars[kBarX], 0, deadline)) {
@@ -552,9 +625,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
         // lane holds experts 8*lane .. 8*lane+7
         float v[8];
         bool ok = !S->abort;
-        if (ok) ok = poll_tagged4(&sy->logits[8 * lane], tag, v, deadline) &&
+        // wait on one word per lane first (light polling), then read the lane's 8 words
+        float probe;
+        if (ok) ok = poll_tagged1(&sy->logits[8 * lane + 7], tag, &probe, deadline) &&
+                     poll_tagged4(&sy->logits[8 * lane], tag, v, deadline) &&
                      poll_tagged4(&sy->logits[8 * lane + 4], tag, v + 4, deadline);
         ok = __all_sync(0xffffffffu, ok);
+        if (lane == 0) NMOE_STAMP(15);
         if (!ok) {
             if (lane == 0 && !S->abort) NMOE_GIVEUP(3);
         } else {
@@ -562,50 +639,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
                 reinterpret_cast<float4 *>(P.logits_out)[2 * lane] = make_float4(v[0], v[1], v[2], v[3]);
                 reinterpret_cast<float4 *>(P.logits_out)[2 * lane + 1] = make_float4(v[4], v[5], v[6], v[7]);
             }
-            // threshold = min over 8 groups (4 lanes = 32 logits) of the group maximum:
-            // at least 8 logits are >= it, so the top-k (k <= 8) are among them.
-            float m = v[0];
-#pragma unroll
-            for (int i = 1; i < 8; ++i) m = fmaxf(m, v[i]);
-            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-            float thr = m;
-            thr = fminf(thr, __shfl_xor_sync(0xffffffffu, thr, 4));
-            thr = fminf(thr, __shfl_xor_sync(0xffffffffu, thr, 8));
-            thr = fminf(thr, __shfl_xor_sync(0xffffffffu, thr, 16));
-            int cnt = 0;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) cnt += !(v[i] < thr);
-            int incl = cnt;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int y = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl += y;
-            }
-            const int nc = __shfl_sync(0xffffffffu, incl, 31);
-            int pos = incl - cnt;
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-                if (!(v[i] < thr)) {
-                    S->cval[pos] = v[i];
-                    S->cidx[pos] = 8 * lane + i;
-                    ++pos;
-                }
-            __syncwarp();
-            for (int q = lane; q < nc; q += 32) {
-                const float vi = S->cval[q];
-                const int ii = S->cidx[q];
-                int rank = 0;
-                for (int j = 0; j < nc; ++j) {
-                    const float u = S->cval[j];
-                    rank += (u > vi) | ((u == vi) & (S->cidx[j] < ii));
-                }
-                if (rank < k) {
-                    S->idx[rank] = (uint32_t)ii;
-                    S->sel_v[rank] = vi;
-                }
-            }
-            __syncwarp();
+            warp_topk(v, k, S, lane);
             if (lane < kMaxK) {
                 const int s = lane;
                 const float l0 = S->sel_v[0];
@@ -637,16 +671,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
                                  pg.bp, &bars[kBarUnit0 + i], pol);
                 }
                 for (int i = 0; i < nB; ++i) {
-                    const int band = band0 + i * G;
                     uint32_t bytes = 0;
                     for (int s = 0; s < k; ++s) bytes += S->valid[s] ? pg.db : 0u;
                     mbar_arrive_expect_tx(&bars[kBarBand0 + i], bytes);
-                    for (int s = 0; s < k; ++s)
-                        if (S->valid[s])
-                            bulk_g2s(sm + Y.bands + (i * Y.kmax + s) * pg.db,
-                                     P.experts + (size_t)S->idx[s] * pg.esz + pg.gu_bytes + (size_t)band * pg.db, pg.db,
-                                     &bars[kBarBand0 + i], pol);
                 }
+                if (nU == 0) issue_bands();
                 if (!P.shared_early) issue_shared();
                 NMOE_STAMP(10);
             }
@@ -691,7 +720,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
                     if (lane == 0) NMOE_GIVEUP(4);
                     break;
                 }
-                if (i == 0 && tid == 0) NMOE_STAMP(11);
+                if (i == 0 && tid == 0) {
+                    NMOE_STAMP(11);
+                    issue_bands();
+                }
                 float g = 0.f, uu = 0.f;
                 if (S->valid[slot]) {
                     const uint8_t *up0 = sm + Y.units + i * pg.bp;
@@ -708,11 +740,23 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
                 }
                 g = warp_sum(g);
                 uu = warp_sum(uu);
-                if (lane == 0)
-                    st_tagged(&sy->act[slot * kInter + band * 16 + warp], S->valid[slot] ? siluf_(g) * uu : 0.f, tag);
+                if (lane == 0) sy->act[slot * kInter + band * 16 + warp] = S->valid[slot] ? siluf_(g) * uu : 0.f;
             }
         }
         __syncthreads();
+        // The next layer's routing-independent weights (router + shared expert) do not
+        // depend on this call: start pulling them into L2 now, so that its head reads L2.
+        if (tid == 0 && P.next_dense) {
+            const uint32_t lo = (uint32_t)(((uint64_t)P.next_dense_bytes * c / G) & ~15ull);
+            const uint32_t hi = (uint32_t)(((uint64_t)P.next_dense_bytes * (c + 1) / G) & ~15ull);
+            if (hi > lo)
+                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(P.next_dense + lo), "r"(hi - lo) : "memory");
+        }
+        // publish: the CTA's act stores happen-before (barrier + fence) the unit flags
+        if (tid < nU) {
+            __threadfence();
+            asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(&sy->uflag[c + tid * G]), "r"(tag) : "memory");
+        }
         if (!P.shared_early) {
             bool ok = true;
             for (int v = warp; ok && v < uS + uG; v += kWarps) ok = do_unit(uR + v);
@@ -770,16 +814,23 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
             }
             __syncthreads();
             if (!S->abort) {
-                // act: poll the tagged words, stage fp32 padded + per-32-column parity sums
+                // act: wait for the 32k unit flags, then stage fp32 padded + parity sums
                 float *asum = reinterpret_cast<float *>(sm + Y.ag);   // [k*16 chunks][3]
+                if (tid < 32 * k) {
+                    bool got = false;
+                    for (uint32_t it = 0; it < kMaxSpins; ++it) {
+                        if (ld_acquire_u32(&sy->uflag[tid]) == tag) { got = true; break; }
+                        if (globaltimer_ns() > deadline) break;
+                        __nanosleep(32);
+                    }
+                    if (!got) NMOE_GIVEUP(6);
+                }
+                __syncthreads();
                 for (int i0 = 0; i0 < k * kInter / 4; i0 += kThreads) {
                     const int i = i0 + tid;
                     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
                     if (i < k * kInter / 4) {
-                        if (!poll_tagged4(&sy->act[4 * i], tag, &v.x, deadline)) {
-                            NMOE_GIVEUP(6);
-                            v = make_float4(0.f, 0.f, 0.f, 0.f);
-                        }
+                        v = __ldcg(reinterpret_cast<const float4 *>(sy->act) + i);
                         const int e = 4 * i;
                         *reinterpret_cast<float4 *>(actf + (e >> 5) * kXP + (e & 31)) = v;
                     }
@@ -909,7 +960,7 @@ struct nmoe::FusedState {
     bool ok = false;
     uint64_t timeout_ns = 1000000000ull;
     int timeline = 0;
-    int shared_early = 0;
+    int shared_early = 1;
     int expert_fp32 = 0;   // NMOE_EXPERT_FP32=1: fp32 routed-expert dots (slower, ~1e-6)
 };
 
@@ -982,6 +1033,7 @@ int nmoe_fused_init(nmoe_moe_ctx *ctx) {
     if (const char *t = getenv("NMOE_WAIT_TIMEOUT_MS")) F->timeout_ns = (uint64_t)atoll(t) * 1000000ull;
     if (const char *t = getenv("NMOE_TIMELINE")) F->timeline = atoi(t) != 0;
     if (const char *t = getenv("NMOE_SHARED_EARLY")) F->shared_early = atoi(t) != 0;
+    F->expert_fp32 = (ctx->cfg.flags & NMOE_FLAG_EXPERT_FP32) != 0;
     if (const char *t = getenv("NMOE_EXPERT_FP32")) F->expert_fp32 = atoi(t) != 0;
     const int bits = ctx->cfg.quant_bits;
     const bool rq4 = ctx->cfg.router_dtype == NMOE_DTYPE_Q4, sq4 = ctx->cfg.shared_dtype == NMOE_DTYPE_Q4;
@@ -1047,6 +1099,8 @@ cudaError_t nmoe_fused_launch(nmoe_moe_ctx *ctx, const FusedCall &a, cudaStream_
     p.num_experts = a.num_experts;
     p.route_only = a.route_only;
     p.shared_early = F->shared_early;
+    p.next_dense = a.next_dense;
+    p.next_dense_bytes = a.next_dense_bytes;
     p.timeline = F->timeline;
     p.sy = F->sy;
     p.err = a.err;

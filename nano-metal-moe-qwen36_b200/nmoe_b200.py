@@ -42,7 +42,9 @@ class Config(C.Structure):
     _fields_ = [("quant_bits", C.c_int), ("num_layers", C.c_int), ("num_experts", C.c_int),
                 ("k_max", C.c_int), ("router_dtype", C.c_int), ("shared_dtype", C.c_int),
                 ("t_max", C.c_int), ("world_size", C.c_int), ("rank", C.c_int),
-                ("nccl_unique_id", C.c_void_p)]
+                ("nccl_unique_id", C.c_void_p), ("flags", C.c_int)]
+
+FLAG_PREFETCH_NEXT_LAYER, FLAG_EXPERT_FP32 = 1, 2
 
 
 class Tensor(C.Structure):
@@ -147,13 +149,13 @@ class Context:
 
     def __init__(self, quant_bits=4, num_layers=1, num_experts=NUM_EXPERTS, k_max=8,
                  router_dtype=DTYPE_BF16, shared_dtype=DTYPE_BF16, t_max=0, device=0,
-                 world_size=1, rank=0, nccl_unique_id: bytes | None = None):
+                 world_size=1, rank=0, nccl_unique_id: bytes | None = None, flags=0):
         self._L = lib()
         self._id_buf = None
         if nccl_unique_id is not None:
             self._id_buf = C.create_string_buffer(bytes(nccl_unique_id), 128)
         self.cfg = Config(quant_bits, num_layers, num_experts, k_max, router_dtype, shared_dtype, t_max,
-                          world_size, rank, C.cast(self._id_buf, C.c_void_p) if self._id_buf else None)
+                          world_size, rank, C.cast(self._id_buf, C.c_void_p) if self._id_buf else None, flags)
         st = C.c_int(0)
         h = self._L.nmoe_moe_create(C.byref(self.cfg), device, C.byref(st))
         if not h:
