@@ -588,7 +588,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
                 const float l0 = S->tk.sel_v[0];
                 float sum = 0.f;
                 for (int t = 0; t < k; ++t) sum += expf(S->tk.sel_v[t] - l0);
-                const uint32_t e = s < k ? S->idx[s] : 0u;
+                const uint32_t e = s < k ? S->tk.idx[s] : 0u;
+                S->idx[s] = e;
                 const float w = s < k ? expf(S->tk.sel_v[s] - l0) / sum : 0.f;
                 const int valid = s < k && e < (uint32_t)P.num_experts;
                 if (s < k && !valid) set_err(P.err, kErrExpertRange);
@@ -598,7 +599,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
                     if (P.idx_out) P.idx_out[s] = e;
                     if (P.w_out) P.w_out[s] = w;
                 }
-                if (s >= k) S->idx[s] = 0u;
             }
             __syncwarp();
             // routed copies: gate/up units, then this CTA's output bands of every slot
