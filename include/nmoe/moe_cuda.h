@@ -188,6 +188,11 @@ int nmoe_moe_debug_trail(nmoe_moe_ctx *ctx, uint32_t *out, int n);
  * the environment. Synchronises the device. */
 int nmoe_moe_debug_timeline(nmoe_moe_ctx *ctx, uint32_t *out, int n_ctas);
 
+/* Diagnostics: copy the router logits [T][256] (fp32) of the last
+ * nmoe_moe_forward_batched call to host memory (T <= that call's T). Synchronises the
+ * device. */
+int nmoe_moe_debug_logits(nmoe_moe_ctx *ctx, float *out, int T);
+
 /* ---- forward without any allocation ------------------------------------------ */
 
 /* No counterpart in the reference. The batch-1 block of nmoe_moe_forward for callers

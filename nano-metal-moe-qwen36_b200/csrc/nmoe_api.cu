@@ -52,27 +52,6 @@ struct DeviceGuard {
     }
 };
 
-static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
-
-// Dense arena of one layer, row-interleaved (nmoe_pack.cuh): router rows, shared
-// gate/up pairs, gate vector, shared down rows; each region 256-byte aligned.
-struct DenseArena {
-    size_t router, spairs, gvec, sdown, total;
-    uint32_t rrow, srow, sdrow;   // row bytes (router, shared gate/up, shared down)
-};
-static DenseArena dense_arena(int router_dtype, int shared_dtype) {
-    DenseArena a;
-    a.rrow = dense_row_bytes(router_dtype == NMOE_DTYPE_Q4, NMOE_HIDDEN);
-    a.srow = dense_row_bytes(shared_dtype == NMOE_DTYPE_Q4, NMOE_HIDDEN);
-    a.sdrow = dense_row_bytes(shared_dtype == NMOE_DTYPE_Q4, NMOE_INTER);
-    a.router = 0;
-    a.spairs = align256(a.router + (size_t)NMOE_NUM_EXPERTS * a.rrow);
-    a.gvec = align256(a.spairs + (size_t)NMOE_INTER * 2 * a.srow);
-    a.sdown = align256(a.gvec + a.srow);
-    a.total = align256(a.sdown + (size_t)NMOE_HIDDEN * a.sdrow);
-    return a;
-}
-
 // ------------------------------------------------------------- host helpers ----
 
 extern "C" size_t nmoe_moe_expert_size(int quant_bits) {

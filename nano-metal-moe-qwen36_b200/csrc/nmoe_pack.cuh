@@ -15,6 +15,7 @@
 // contiguous copy: router rows [w | s | b] (q4) or [w] (bf16); shared gate/up pairs
 // [gate.w | up.w | gate.s | gate.b | up.s | up.b]; shared down rows [w | s | b].
 #pragma once
+#include <stddef.h>
 #include <stdint.h>
 
 namespace nmoe {
@@ -47,6 +48,27 @@ __host__ __device__ inline PackGeo pack_geo(int bits) {
 // Dense row/pair strides in the repacked dense arena.
 __host__ __device__ inline uint32_t dense_row_bytes(bool q4, int cols) {
     return q4 ? (uint32_t)(cols / 2 + 2 * (cols / 64) * 2) : (uint32_t)(cols * 2);
+}
+
+inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+// Dense arena of one layer, row-interleaved as above: router rows, shared
+// gate/up pairs, gate vector, shared down rows; each region 256-byte aligned.
+struct DenseArena {
+    size_t router, spairs, gvec, sdown, total;
+    uint32_t rrow, srow, sdrow;   // row bytes (router, shared gate/up, shared down)
+};
+inline DenseArena dense_arena(int router_dtype, int shared_dtype) {
+    DenseArena a;
+    a.rrow = dense_row_bytes(router_dtype == 4, 2048);
+    a.srow = dense_row_bytes(shared_dtype == 4, 2048);
+    a.sdrow = dense_row_bytes(shared_dtype == 4, 512);
+    a.router = 0;
+    a.spairs = align256(a.router + (size_t)256 * a.rrow);
+    a.gvec = align256(a.spairs + (size_t)512 * 2 * a.srow);
+    a.sdown = align256(a.gvec + a.srow);
+    a.total = align256(a.sdown + (size_t)2048 * a.sdrow);
+    return a;
 }
 
 }  // namespace nmoe

@@ -29,6 +29,7 @@ ABI_SYMBOLS = (
     "nmoe_moe_load_layer", "nmoe_moe_load_layer_file", "nmoe_moe_set_dense",
     "nmoe_moe_forward", "nmoe_moe_route", "nmoe_moe_forward_batched", "nmoe_moe_device_status",
     "nmoe_moe_forward_static", "nmoe_moe_static_error", "nmoe_moe_debug_trail", "nmoe_moe_debug_timeline",
+    "nmoe_moe_debug_logits",
 )
 
 
@@ -109,6 +110,8 @@ def lib() -> C.CDLL:
     L.nmoe_moe_debug_trail.argtypes = [vp, vp, i]
     L.nmoe_moe_debug_timeline.restype = i
     L.nmoe_moe_debug_timeline.argtypes = [vp, vp, i]
+    L.nmoe_moe_debug_logits.restype = i
+    L.nmoe_moe_debug_logits.argtypes = [vp, vp, i]
     _lib = L
     return L
 
@@ -212,6 +215,12 @@ class Context:
                         idx_out=None, w_out=None, stream=0):
         self._check(self._L.nmoe_moe_forward_batched(self.h, layer, T, k, _ptr(x), x_dtype, _ptr(h_mid), _ptr(out),
                                                      out_dtype, _ptr(idx_out), _ptr(w_out), stream))
+
+    def debug_logits(self, T):
+        """Router logits [T][256] of the last forward_batched call."""
+        out = np.zeros((T, 256), np.float32)
+        self._check(self._L.nmoe_moe_debug_logits(self.h, out.ctypes.data, T))
+        return out
 
     def debug_trail(self, n=1024):
         out = np.zeros(n, np.uint32)
