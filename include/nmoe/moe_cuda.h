@@ -192,6 +192,11 @@ int nmoe_moe_debug_timeline(nmoe_moe_ctx *ctx, uint32_t *out, int n_ctas);
  * nmoe_moe_forward_batched call to host memory (T <= that call's T). Synchronises the
  * device. */
 int nmoe_moe_debug_logits(nmoe_moe_ctx *ctx, float *out, int T);
+/* Diagnostics: per-role %clock timestamps of CTA 0 of one grouped-GEMM launch of
+ * nmoe_moe_forward_batched ([13][1024] u32: producer slots, B stages, dequant start/end,
+ * MMA issue, epilogue start/end, raw slot landed, MMA step issued, last dequant warp step end, dequant wait begin, A stage free, scales ready), recorded when the context was created with
+ * NMOE_GEMM_TRACE=<0 router | 1 gate/up | 2 down> in the environment. */
+int nmoe_moe_debug_gemm_trace(nmoe_moe_ctx *ctx, uint32_t *out, int n);
 
 /* ---- forward without any allocation ------------------------------------------ */
 

@@ -4,13 +4,15 @@
 // (src/runtime.m:3816); this path computes the same block for T tokens at once:
 //
 //   k_prep      x -> bf16 hi (and lo, for f32 x) planes in the K order of the GEMM
-//   GEMM        router logits [T][256] (hi/lo split operands: fp32-accurate)
+//   GEMM        router logits [T][256] (hi/lo split operands: fp32-accurate), K-slice
+//               partial sums when T is small so that the router spreads over the SMs
 //   k_route     per token: top-k of 256 + renormalised weights (src/runtime.m:1498-1511),
 //               shared-gate score, per-expert counts and ranks
 //   k_scatter   positions: tokens grouped by expert (offset[e] + rank)
-//   GEMM        gate/up + SwiGLU for every (token, expert) position and for the shared
-//               expert over all T tokens -> act
-//   GEMM        down -> Y per position
+//   GEMM        gate/up + SwiGLU for every (token, expert) position -> act; the shared
+//               expert's gate/up over all T tokens as K-slice partials
+//   k_shared_act  shared SiLU(gate) * up -> act
+//   GEMM        down -> Y per routed position; shared down as K-slice partials
 //   k_combine   out = h_mid + sum_s w_s Y[pos(t,s)] + sigmoid(score) * Y[shared(t)]
 //               (nmoe_expert_down_combine_q4, metal/kernels.metal:1497-1541)
 // Every launch is asynchronous on the caller's stream; nothing is allocated per call.
@@ -34,6 +36,7 @@ namespace nmoe {
 struct BatchedState {
     int t_max = 0;
     uint16_t *xh = nullptr, *xl = nullptr;   // [t_max][2048] K-permuted bf16 planes
+    uint16_t *xp = nullptr;                  // [t_max * 8][2048] xh rows in position order
     float *logits = nullptr;                 // [t_max][256]
     float *score = nullptr;                  // [t_max]
     float *w = nullptr;                      // [t_max][8]
@@ -42,10 +45,17 @@ struct BatchedState {
     int *perm = nullptr;                     // [t_max * 8]
     int *cnt = nullptr;                      // [256]
     uint16_t *act = nullptr;                 // [t_max * 9][512]  (routed positions, then shared)
-    uint16_t *y = nullptr;                   // [t_max * 9][2048]
+    uint16_t *y = nullptr;                   // [t_max * 8][2048] routed down outputs
+    int rows_cap = 0;                        // rows of each partial-sum buffer
+    float *p_router = nullptr;               // [rows_cap][256]   router K-slice partials
+    float *p_sgu = nullptr;                  // [rows_cap][1024]  shared gate|up partials
+    float *p_sdown = nullptr;                // [rows_cap][2048]  shared down partials
     PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
     uint64_t timeout_ns = 1000000000ull;
     int last_T = 0;
+    int trace_launch = -1;                   // NMOE_GEMM_TRACE=<0 router | 1 gate/up | 2 down>
+    uint32_t *trace = nullptr;               // [kTraceRows][1024]
+    int launch_no = 0;
 };
 
 }  // namespace nmoe
@@ -81,7 +91,9 @@ __global__ void k_prep(const void *x, int x_f32, int T, uint16_t *xh, uint16_t *
 // One warp per token: top-k of the 256 logits, renormalised weights, shared-gate score
 // (fp32, from the unpermuted x), ranks within each expert's group.
 struct RouteArgs {
-    const float *logits;
+    const float *part;        // router partial sums [nsplit][T][256]
+    int nsplit;
+    float *logits;            // their sum [T][256]
     const void *x;
     int x_f32;
     const uint8_t *gvec;
@@ -104,10 +116,16 @@ __global__ void __launch_bounds__(kRouteWarps * 32) k_route(const RouteArgs a) {
     const int t = blockIdx.x * kRouteWarps + warp;
     if (t >= a.T) return;
     TopkScratch *S = &tk[warp];
-    float v[8];
-    const float4 *lg = reinterpret_cast<const float4 *>(a.logits + (size_t)t * kExperts + 8 * lane);
-    const float4 l0 = lg[0], l1 = lg[1];
-    v[0] = l0.x; v[1] = l0.y; v[2] = l0.z; v[3] = l0.w; v[4] = l1.x; v[5] = l1.y; v[6] = l1.z; v[7] = l1.w;
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+    for (int sp = 0; sp < a.nsplit; ++sp) {   // K slices summed in a fixed order
+        const float4 *lg = reinterpret_cast<const float4 *>(a.part + ((size_t)sp * a.T + t) * kExperts + 8 * lane);
+        const float4 l0 = lg[0], l1 = lg[1];
+        v[0] += l0.x; v[1] += l0.y; v[2] += l0.z; v[3] += l0.w; v[4] += l1.x; v[5] += l1.y; v[6] += l1.z; v[7] += l1.w;
+    }
+    float4 *lo = reinterpret_cast<float4 *>(a.logits + (size_t)t * kExperts + 8 * lane);
+    lo[0] = make_float4(v[0], v[1], v[2], v[3]);
+    lo[1] = make_float4(v[4], v[5], v[6], v[7]);
     warp_topk(v, a.k, S, lane);
 
     // shared-gate score: lane covers columns 64*lane .. 64*lane+63
@@ -205,9 +223,54 @@ __global__ void k_scatter(const uint32_t *idx, const int *rank, const int *cnt, 
     inv[(size_t)t * kMaxK + s] = pos;
 }
 
-// out[t][c..c+8) = h_mid + sum_s w_s * Y[pos(t,s)] + sigmoid(score_t) * Y[shared(t)]
+// xp[pos] = xh[perm[pos]]: each routed token's row at its position, 16 bytes a thread.
+// Positions past the routed total (possible only after an out-of-range expert id) copy
+// a stale but in-range row that no item reads.
+__global__ void k_gather_rows(const uint16_t *xh, const int *perm, int T, int k, uint16_t *xp) {
+    const int pos = blockIdx.x, c = threadIdx.x;
+    if (pos >= T * k) return;
+    reinterpret_cast<uint4 *>(xp + (size_t)pos * kHidden)[c] =
+        reinterpret_cast<const uint4 *>(xh + (size_t)perm[pos] * kHidden)[c];
+}
+
+// Shared expert: act[shared_base + t] = SiLU(gate) * up from the K-slice partial sums
+// [nsplit][T][gate 512 | up 512], written in the GEMM's K order.
+__global__ void k_shared_act(const float *part, int nsplit, int T, uint16_t *act, int shared_base) {
+    // four lanes per (token, 8-row group) share the K slices, then add in a fixed order
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    const int q = i & 3, grp = i >> 2;
+    const bool live = grp < T * (kInter / 8);
+    const int t = live ? grp / (kInter / 8) : 0, j0 = live ? (grp % (kInter / 8)) * 8 : 0;
+    float g[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, u[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (live) {
+#pragma unroll 4
+        for (int sp = q; sp < nsplit; sp += 4) {
+            const float4 *r = reinterpret_cast<const float4 *>(part + ((size_t)sp * T + t) * (2 * kInter) + j0);
+            const float4 a = r[0], b = r[1], c = r[kInter / 4], d = r[kInter / 4 + 1];
+            g[0] += a.x; g[1] += a.y; g[2] += a.z; g[3] += a.w; g[4] += b.x; g[5] += b.y; g[6] += b.z; g[7] += b.w;
+            u[0] += c.x; u[1] += c.y; u[2] += c.z; u[3] += c.w; u[4] += d.x; u[5] += d.y; u[6] += d.z; u[7] += d.w;
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        g[j] += __shfl_xor_sync(0xffffffffu, g[j], 1);
+        u[j] += __shfl_xor_sync(0xffffffffu, u[j], 1);
+        g[j] += __shfl_xor_sync(0xffffffffu, g[j], 2);
+        u[j] += __shfl_xor_sync(0xffffffffu, u[j], 2);
+    }
+    if (!live || q != 0) return;
+    float a[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) a[j] = g[j] / (1.f + expf(-g[j])) * u[j];
+    // K order [0,4,1,5,2,6,3,7]
+    reinterpret_cast<uint4 *>(act + (size_t)(shared_base + t) * kInter + j0)[0] =
+        make_uint4(pack_bf16x2(a[0], a[4]), pack_bf16x2(a[1], a[5]), pack_bf16x2(a[2], a[6]), pack_bf16x2(a[3], a[7]));
+}
+
+// out[t][c..c+8) = h_mid + sum_s w_s * Y[pos(t,s)] + sigmoid(score_t) * shared_down(t), the
+// shared down from its K-slice partial sums [nsplit][T][2048].
 __global__ void k_combine(const uint16_t *y, const float *w, const int *inv, const float *score, const float *h_mid,
-                          int T, int k, int shared_base, void *out, int out_bf16) {
+                          const float *sdown, int nsplit, int T, int k, void *out, int out_bf16) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;   // 8-column chunk
     if (i >= T * (kHidden / 8)) return;
     const int t = i >> 8, c = (i & 255) * 8;
@@ -225,14 +288,15 @@ __global__ void k_combine(const uint16_t *y, const float *w, const int *inv, con
         }
     }
     const float sg = 1.f / (1.f + expf(-score[t]));
-    const uint4 q = *reinterpret_cast<const uint4 *>(y + (size_t)(shared_base + t) * kHidden + c);
-    const uint32_t u[4] = {q.x, q.y, q.z, q.w};
-    float o[8];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        o[2 * j] = sg * bf16_lo(u[j]);
-        o[2 * j + 1] = sg * bf16_hi(u[j]);
+    float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+    for (int sp = 0; sp < nsplit; ++sp) {
+        const float4 *r = reinterpret_cast<const float4 *>(sdown + ((size_t)sp * T + t) * kHidden + c);
+        const float4 a = r[0], b = r[1];
+        o[0] += a.x; o[1] += a.y; o[2] += a.z; o[3] += a.w; o[4] += b.x; o[5] += b.y; o[6] += b.z; o[7] += b.w;
     }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] *= sg;
     float hm[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     if (h_mid) {
         const float4 a = reinterpret_cast<const float4 *>(h_mid + (size_t)t * kHidden + c)[0];
@@ -270,18 +334,35 @@ struct Guard {
 
 constexpr int kGemmSmemMax = 227 * 1024;
 
-// 4D tiled map: (inner elements, 16 rows, bands, groups); box (box0, 16, 8, 1).
+// 4D tiled map: (inner elements, 16 rows, bands, groups); box (box0, 16, box2, 1).
 bool make_map(BatchedState *B, CUtensorMap *m, const void *base, bool u32, uint64_t d0, uint64_t row_stride,
-              uint64_t bands, uint64_t band_stride, uint64_t groups, uint64_t group_stride, uint32_t box0) {
+              uint64_t bands, uint64_t band_stride, uint64_t groups, uint64_t group_stride, uint32_t box0,
+              uint32_t box2 = 8) {
     const cuuint64_t dims[4] = {d0, 16, bands, groups};
     const cuuint64_t strides[3] = {row_stride, band_stride, group_stride};
-    const cuuint32_t box[4] = {box0, 16, 8, 1};
+    const cuuint32_t box[4] = {box0, 16, box2, 1};
     const cuuint32_t es[4] = {1, 1, 1, 1};
     const CUresult r = B->encode(m, u32 ? CU_TENSOR_MAP_DATA_TYPE_UINT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16, 4,
                                  const_cast<void *>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
                                  CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
+}
+
+// B rows: 2D (K columns, rows) bf16, box 64 columns x 16 rows, 128B swizzle.
+bool make_bmap(BatchedState *B, CUtensorMap *m, const uint16_t *base, int K, int rows) {
+    if (base == nullptr) return true;
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    const cuuint32_t box[2] = {64, 16};
+    const cuuint32_t es[2] = {1, 1};
+    return B->encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint16_t *>(base), dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool make_bmaps(BatchedState *B, GemmProblem &pr, int rows) {
+    return make_bmap(B, &pr.tx[0], pr.b_hi, pr.K, rows) && make_bmap(B, &pr.tx[1], pr.b_lo, pr.K, rows);
 }
 
 // Weight (+ scale/bias) maps of one q4/q2/bf16 matrix whose rows are `row_stride` bytes
@@ -291,27 +372,48 @@ bool make_map(BatchedState *B, CUtensorMap *m, const void *base, bool u32, uint6
 bool make_matrix_maps(BatchedState *B, GemmProblem &pr, int m, const uint8_t *base, int fmt, int cols,
                       uint64_t row_stride, uint64_t bands, uint64_t band_stride, uint64_t groups, uint64_t group_stride,
                       size_t s_off, size_t b_off, uint64_t s_row_stride) {
+    // box: one raw slot (step_geo): q formats sps steps x 128 rows, bf16 a block of rows
+    const StepGeo G = step_geo(fmt, pr.n_mat, cols, 1);
     if (fmt == kAFmtBf16)
-        return make_map(B, &pr.tw[m], base, false, cols, row_stride, bands, band_stride, groups, group_stride, 64);
+        return make_map(B, &pr.tw[m], base, false, cols, row_stride, bands, band_stride, groups, group_stride, 64,
+                        8 / G.nslot);
     const int vpw = fmt == kAFmtQ4 ? 8 : 16;
     const int ng = cols / 64;
     return make_map(B, &pr.tw[m], base, true, cols / vpw, row_stride, bands, band_stride, groups, group_stride,
-                    64 / vpw) &&
+                    G.wpk * G.sps) &&
            make_map(B, &pr.ts[m], base + s_off, false, ng, s_row_stride, bands, band_stride, groups, group_stride, 8) &&
            make_map(B, &pr.tb[m], base + b_off, false, ng, s_row_stride, bands, band_stride, groups, group_stride, 8);
 }
 
 cudaError_t launch_gemm(nmoe_moe_ctx *ctx, GemmParams &P, cudaStream_t st) {
-    int raw = 0;
-    for (int i = 0; i < P.n_prob; ++i) raw = max(raw, P.prob[i].n_mat * raw_mat_bytes(P.prob[i].fmt));
-    P.raw_stage = raw;
-    P.sr = std::min(8, std::max(2, 65536 / raw));
+    int sr = kGemmMaxSlots;
+    while (sr > 2 && gemm_smem_bytes(sr) > (size_t)kGemmSmemMax) --sr;
+    P.sr = sr;
+    P.acc_bufs = 2;
+    for (int i = 0; i < P.n_prob; ++i)
+        if (P.prob[i].n_mat == 2) P.acc_bufs = 1;
     P.err = ctx->d_err;
     P.timeout_ns = ctx->batched->timeout_ns;
-    const size_t smem = 1024 + kGemmSA * 2 * kGemmAStage + kGemmSB * kGemmBStage + kGemmSS * 2 * kGemmScStage +
-                        (size_t)P.sr * raw + sizeof(GemmSmem);
-    k_moe_gemm<<<ctx->num_sms, kGemmThreads, smem, st>>>(P);
+    BatchedState *B = ctx->batched;
+    P.trace = (B->trace && B->launch_no == B->trace_launch) ? B->trace : nullptr;
+    ++B->launch_no;
+    k_moe_gemm<<<ctx->num_sms, kGemmThreads, gemm_smem_bytes(sr), st>>>(P);
     return cudaGetLastError();
+}
+
+// K slices for a dense problem over T tokens: enough items to cover the SMs, within
+// the partial-sum buffer (rows_cap rows) and the slot geometry.
+int pick_ksplit(int fmt, int n_mat, int K, int m_tiles, int T, int rows_cap, int target) {
+    const int chunks = (T + kGemmNChunk - 1) / kGemmNChunk;
+    int best = 1;
+    for (int S = 2; S <= 32; S *= 2) {
+        if ((K / 64) % S) break;
+        const StepGeo G = step_geo(fmt, n_mat, K, S);
+        if (G.kb < 1 || G.kb % G.sps || (long)S * T > rows_cap) break;
+        if (m_tiles * chunks * best >= target) break;
+        best = S;
+    }
+    return best;
 }
 
 }  // namespace
@@ -334,17 +436,27 @@ int nmoe_batched_init(nmoe_moe_ctx *ctx) {
         nmoe_ctx_set_error(ctx, "gemm smem attribute: %s", cudaGetErrorString(e));
         return NMOE_ECUDA;
     }
+    if (const char *t = getenv("NMOE_GEMM_TRACE")) {
+        B->trace_launch = atoi(t);
+        if (cudaMalloc(&B->trace, kTraceRows * kTraceRow * 4) != cudaSuccess) B->trace = nullptr;
+        else cudaMemset(B->trace, 0, kTraceRows * kTraceRow * 4);
+    }
     const int tm = ctx->cfg.t_max;
     B->t_max = tm;
     if (tm <= 0) return NMOE_OK;
     const size_t T = (size_t)tm;
+    B->rows_cap = std::max(4 * tm, 1024);
+    const size_t R = (size_t)B->rows_cap;
     struct { void **p; size_t bytes; } al[] = {
         {(void **)&B->xh, T * kHidden * 2},       {(void **)&B->xl, T * kHidden * 2},
+        {(void **)&B->xp, T * kMaxK * kHidden * 2},
         {(void **)&B->logits, T * kExperts * 4},  {(void **)&B->score, T * 4},
         {(void **)&B->w, T * kMaxK * 4},          {(void **)&B->idx, T * kMaxK * 4},
         {(void **)&B->rank, T * kMaxK * 4},       {(void **)&B->inv, T * kMaxK * 4},
         {(void **)&B->perm, T * kMaxK * 4},       {(void **)&B->cnt, kExperts * 4},
-        {(void **)&B->act, T * 9 * kInter * 2},   {(void **)&B->y, T * 9 * kHidden * 2},
+        {(void **)&B->act, T * 9 * kInter * 2},   {(void **)&B->y, T * 8 * kHidden * 2},
+        {(void **)&B->p_router, R * kExperts * 4}, {(void **)&B->p_sgu, R * 2 * kInter * 4},
+        {(void **)&B->p_sdown, R * kHidden * 4},
     };
     for (auto &a : al) {
         e = cudaMalloc(a.p, a.bytes);
@@ -360,7 +472,9 @@ int nmoe_batched_init(nmoe_moe_ctx *ctx) {
 void nmoe_batched_destroy(nmoe_moe_ctx *ctx) {
     BatchedState *B = ctx->batched;
     if (B == nullptr) return;
-    void *ps[] = {B->xh, B->xl, B->logits, B->score, B->w, B->idx, B->rank, B->inv, B->perm, B->cnt, B->act, B->y};
+    void *ps[] = {B->xh,   B->xl,  B->xp,  B->logits, B->score, B->w,        B->idx,  B->rank,
+                  B->inv,  B->perm, B->cnt,   B->act,   B->y,        B->p_router, B->p_sgu, B->p_sdown,
+                  B->trace};
     for (void *p : ps)
         if (p) cudaFree(p);
     delete B;
@@ -395,6 +509,7 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
         return NMOE_EINVAL;
     }
     B->last_T = T;
+    B->launch_no = 0;
     if (T == 0) return NMOE_OK;
     Guard guard(ctx->device);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -411,7 +526,13 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
     // 1. x planes, counts cleared
     k_prep<<<(T * 256 + 255) / 256, 256, 0, st>>>(x, xf32, T, B->xh, B->xl, B->cnt);
 
-    // 2. router logits
+    // K slices of the dense problems (router, shared gate/up, shared down)
+    const int target = ctx->num_sms;
+    const int nsplit_r = pick_ksplit(rfmt, 1, kHidden, 2, T, B->rows_cap, target);
+    const int nsplit_g = pick_ksplit(sfmt, 2, kHidden, 4, T, B->rows_cap, target);
+    const int nsplit_d = pick_ksplit(sfmt, 1, kInter, 16, T, B->rows_cap, target);
+
+    // 2. router logits (K-slice partials)
     {
         GemmParams P;
         memset(&P, 0, sizeof P);
@@ -429,9 +550,13 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
         r.split = 1;
         r.epi = kEpiF32;
         r.ld_out = kExperts;
-        r.out = B->logits;
+        r.out = B->p_router;
+        r.ksplit = nsplit_r;
+        r.split_rows = T;
         const uint8_t *rb = dense + DA.router;
-        if (!make_matrix_maps(B, r, 0, rb, rfmt, kHidden, DA.rrow, 16, 16ull * DA.rrow, 1, 256ull * DA.rrow, 1024, 1088, DA.rrow)) {
+        if (!make_matrix_maps(B, r, 0, rb, rfmt, kHidden, DA.rrow, 16, 16ull * DA.rrow, 1, 256ull * DA.rrow, 1024, 1088,
+                              DA.rrow) ||
+            !make_bmaps(B, r, B->t_max)) {
             nmoe_ctx_set_error(ctx, "router tensor map");
             return NMOE_ECUDA;
         }
@@ -444,6 +569,8 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
     // 3. routing
     {
         RouteArgs a;
+        a.part = B->p_router;
+        a.nsplit = nsplit_r;
         a.logits = B->logits;
         a.x = x;
         a.x_f32 = xf32;
@@ -465,6 +592,7 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
         k_route<<<(T + kRouteWarps - 1) / kRouteWarps, kRouteWarps * 32, 0, st>>>(a);
         k_scatter<<<(T * k + 255) / 256, 256, 0, st>>>(B->idx, B->rank, B->cnt, T, k, ctx->expert_lo, ctx->n_local,
                                                        B->perm, B->inv);
+        k_gather_rows<<<T * k, 256, 0, st>>>(B->xh, B->perm, T, k, B->xp);
     }
     const int shared_base = T * k;
 
@@ -478,10 +606,10 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
         r.n_mat = 2;
         r.K = kHidden;
         r.m_tiles = 4;
+        r.ksplit = 1;
         r.n_groups = ctx->n_local;
         r.cnt = B->cnt;
-        r.perm = B->perm;
-        r.b_hi = B->xh;
+        r.b_hi = B->xp;
         r.passes = kPassHiHi;
         r.epi = kEpiSwiGLU;
         r.ld_out = kInter;
@@ -496,14 +624,16 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
         s.n_mat = 2;
         s.K = kHidden;
         s.m_tiles = 4;
+        s.ksplit = nsplit_g;
         s.n_groups = 1;
         s.cnt_const = T;
         s.b_hi = B->xh;
         s.passes = kPassHiHi;
-        s.epi = kEpiSwiGLU;
-        s.ld_out = kInter;
-        s.out = B->act;
-        s.out_base = shared_base;
+        s.epi = kEpiF32;
+        s.ld_out = 2 * kInter;
+        s.mat_col = kInter;
+        s.split_rows = T;
+        s.out = B->p_sgu;
         const uint8_t *sp = dense + DA.spairs;
         const uint64_t ps = 2ull * DA.srow;   // pair stride
         if (sfmt == kAFmtQ4) {
@@ -514,6 +644,7 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
             ok = ok && make_matrix_maps(B, s, 0, sp, sfmt, kHidden, ps, 32, 16 * ps, 1, 512 * ps, 0, 0, ps);
             ok = ok && make_matrix_maps(B, s, 1, sp + DA.srow, sfmt, kHidden, ps, 32, 16 * ps, 1, 512 * ps, 0, 0, ps);
         }
+        ok = ok && make_bmaps(B, r, kMaxK * B->t_max) && make_bmaps(B, s, B->t_max);
         if (!ok) {
             nmoe_ctx_set_error(ctx, "gate/up tensor maps");
             return NMOE_ECUDA;
@@ -523,6 +654,9 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
             return NMOE_ECUDA;
         }
     }
+
+    // shared expert activations from the gate/up partials
+    k_shared_act<<<(T * (kInter / 8) * 4 + 255) / 256, 256, 0, st>>>(B->p_sgu, nsplit_g, T, B->act, shared_base);
 
     // 5. down: routed positions and the shared expert
     {
@@ -534,6 +668,7 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
         r.n_mat = 1;
         r.K = kInter;
         r.m_tiles = 16;
+        r.ksplit = 1;
         r.n_groups = ctx->n_local;
         r.cnt = B->cnt;
         r.b_hi = B->act;
@@ -548,17 +683,19 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
         s.n_mat = 1;
         s.K = kInter;
         s.m_tiles = 16;
+        s.ksplit = nsplit_d;
         s.n_groups = 1;
         s.cnt_const = T;
         s.in_base = shared_base;
-        s.out_base = shared_base;
         s.b_hi = B->act;
         s.passes = kPassHiHi;
-        s.epi = kEpiBf16;
+        s.epi = kEpiF32;
         s.ld_out = kHidden;
-        s.out = B->y;
+        s.split_rows = T;
+        s.out = B->p_sdown;
         const uint64_t rs = DA.sdrow;
         ok = ok && make_matrix_maps(B, s, 0, dense + DA.sdown, sfmt, kInter, rs, 128, 16 * rs, 1, 2048 * rs, 256, 272, rs);
+        ok = ok && make_bmaps(B, r, 9 * B->t_max) && make_bmaps(B, s, 9 * B->t_max);
         if (!ok) {
             nmoe_ctx_set_error(ctx, "down tensor maps");
             return NMOE_ECUDA;
@@ -570,8 +707,8 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
     }
 
     // 6. combine
-    k_combine<<<(T * 256 + 255) / 256, 256, 0, st>>>(B->y, B->w, B->inv, B->score, h_mid, T, k, shared_base, out,
-                                                     out_dtype == NMOE_DTYPE_BF16);
+    k_combine<<<(T * 256 + 255) / 256, 256, 0, st>>>(B->y, B->w, B->inv, B->score, h_mid, B->p_sdown, nsplit_d, T, k,
+                                                     out, out_dtype == NMOE_DTYPE_BF16);
     if ((e = cudaGetLastError()) != cudaSuccess) {
         nmoe_ctx_set_error(ctx, "batched launch: %s", cudaGetErrorString(e));
         return NMOE_ECUDA;
@@ -590,5 +727,16 @@ extern "C" int nmoe_moe_debug_logits(nmoe_moe_ctx *ctx, float *out, int T) {
         nmoe_ctx_set_error(ctx, "debug_logits: %s", cudaGetErrorString(e));
         return NMOE_ECUDA;
     }
+    return NMOE_OK;
+}
+
+extern "C" int nmoe_moe_debug_gemm_trace(nmoe_moe_ctx *ctx, uint32_t *out, int n) {
+    if (ctx == nullptr || ctx->batched == nullptr || ctx->batched->trace == nullptr || out == nullptr || n < 0 ||
+        n > kTraceRows * kTraceRow) {
+        if (ctx) nmoe_ctx_set_error(ctx, "debug_gemm_trace: tracing is off (NMOE_GEMM_TRACE) or bad arguments");
+        return NMOE_EINVAL;
+    }
+    Guard guard(ctx->device);
+    if (cudaMemcpy(out, ctx->batched->trace, (size_t)n * 4, cudaMemcpyDeviceToHost) != cudaSuccess) return NMOE_ECUDA;
     return NMOE_OK;
 }

@@ -2,12 +2,14 @@
 //
 // D[m][n] = sum_k A[m][k] * B[n][k] per work item, where
 //   A = 128 rows of a weight matrix (an expert's gate/up or down rows, the router, the
-//       shared expert), read from HBM in its stored format (q4 / q2 / bf16) by TMA and
-//       dequantised to bf16 in shared memory by a dequant warpgroup;
-//   B = up to 128 token rows (the tokens routed to one expert, in position order),
-//       gathered with cp.async into 128B-swizzled shared memory;
-//   D = fp32 in tensor memory (TMEM), double-buffered so the epilogue of one item
-//       overlaps the main loop of the next.
+//       shared expert), read from HBM in its stored format (q4 / q2 / bf16) by TMA,
+//       dequantised to bf16 by two dequant warpgroups and written straight into tensor
+//       memory (tcgen05.st), where the MMA reads it: no bf16 tile crosses shared memory;
+//   B = up to 128 token rows (the tokens routed to one expert, contiguous in position
+//       order), loaded by TMA into 128B-swizzled shared memory;
+//   D = fp32 in tensor memory (TMEM columns 0-255): one buffer for gate+up items, two
+//       (so the epilogue overlaps the next item) for single-matrix items. Columns 256-511
+//       hold four A stages of 2 x 32 columns.
 // This is the swap-AB form of the reference's per-token expert matvecs
 // (nmoe_expert_gate_up_q4_batched, metal/kernels.metal:562-640; expert down,
 // kernels.metal:642-714): weights are the MMA's M side, tokens its N side, so a group of
@@ -21,8 +23,9 @@
 // Warp roles (512 threads, one CTA per SM, persistent over the item list):
 //   warp 0      TMA producer: raw weight tiles + scale/bias tiles
 //   warp 1      MMA issuer (one thread) and TMEM owner
-//   warps 2-3   B loader: cp.async gather of token rows
-//   warps 4-11  dequant: raw tile -> bf16 swizzled A tile
+//   warp 2      B loader: TMA tiles of token rows (16 rows x 64 columns)
+//   warp 3      idle
+//   warps 4-11  dequant: raw tile -> bf16 A rows in TMEM
 //   warps 12-15 epilogue: TMEM -> registers -> SwiGLU / store
 // Every mbarrier wait is bounded; on timeout the CTA records kErrTimeout, drains what it
 // has in flight (bounded), frees TMEM and exits.
@@ -42,42 +45,66 @@ constexpr int kGemmThreads = 512;
 constexpr int kGemmNChunk = 128;       // tokens per item (MMA N <= 128)
 constexpr int kGemmMaxGroups = 256;
 constexpr int kGemmMaxProblems = 2;
-constexpr int kGemmSA = 2, kGemmSB = 4, kGemmSS = 2;
-constexpr int kGemmAStage = 16384;     // one matrix's 128 x 64 bf16 tile
+constexpr int kGemmSA = 4, kGemmSB = 4, kGemmSS = 2;   // kGemmSS scale stages per dequant group
+constexpr int kGemmMaxSlots = 16;
+constexpr uint32_t kGemmAccCols = 256; // accumulators: TMEM columns [0, 256)
+constexpr uint32_t kGemmACols = 64;    // one A stage: 2 matrices x 32 columns (bf16 pairs)
 constexpr int kGemmBStage = 16384;     // 128 tokens x 64 bf16
 constexpr int kGemmScStage = 4096;     // one matrix's scales + biases, 128 rows x 8 groups
+constexpr int kGemmSlot = 8192;        // raw weight slot
+// Raw weight slots: a q4/q2 slot holds one 64-column step of all 128 rows (8 KB for q4
+// gate+up, less otherwise); a bf16 step spans `nslot` slots, each holding a block of rows
+// (gate+up: 4 x 32 rows, single: 2 x 64).
 
 struct alignas(64) GemmProblem {
     CUtensorMap tw[2];        // weights (4D: inner, 16 rows, bands, group)
     CUtensorMap ts[2];        // scales  (4D: groups, 16 rows, bands, group)
     CUtensorMap tb[2];        // biases
+    CUtensorMap tx[2];        // B rows (2D: K columns, rows; box 64 x 16, 128B swizzle): hi, lo
     int fmt;                  // kAFmt*
-    int n_mat;                // 2 = gate+up (SwiGLU epilogue), 1 otherwise
+    int n_mat;                // 2 = gate+up, 1 otherwise
     int K;                    // 2048 or 512
     int m_tiles;              // rows / 128
+    int ksplit;               // K slices per tile (partial sums, kEpiF32 only)
     int n_groups;             // experts (or 1)
     int cnt_const;            // group size when cnt == nullptr
     const int *cnt;           // [n_groups] tokens per group
-    const int *perm;          // B row of position p, or nullptr (identity)
-    int in_base;              // added to the position before perm / identity
-    int out_base;             // output row = out_base + position
-    const uint16_t *b_hi;     // B rows [.][K] bf16, K-permuted
-    const uint16_t *b_lo;     // low plane for kPassHiLo
+    int in_base;              // B row of position p = in_base + p
+    int out_base;             // output row = out_base + position (+ split * split_rows)
+    int split_rows;
+    const uint16_t *b_hi;     // B rows [.][K] bf16, K-permuted (tx[0])
+    const uint16_t *b_lo;     // low plane for kPassHiLo (tx[1])
     int passes;               // kPass* bits
     int split;                // A in fp32-exact hi/lo planes (router)
     int epi;                  // kEpi*
     int ld_out;
+    int mat_col;              // kEpiF32 with two matrices: column offset of the second
     void *out;
 };
 
 struct GemmParams {
     GemmProblem prob[kGemmMaxProblems];
     int n_prob;
-    int sr;                   // raw stages
-    int raw_stage;            // bytes per raw stage
+    int sr;                   // raw slots
+    int acc_bufs;             // accumulator buffers: 1 when a problem has two matrices, else 2
     int *err;
     uint64_t timeout_ns;
+    uint32_t *trace;          // diagnostics: CTA 0 role timestamps (%clock), or nullptr
 };
+
+// Trace rows (1024 entries each): 0 producer slot acquired, 1 B stage issued, 2 dequant
+// step start, 3 dequant step end, 4 MMA step issued, 5 epilogue item start, 6 item end,
+// 7 raw slot data landed, 8 MMA step B ready, 9 dequant step end (last warp), 10 dequant
+// step begins waiting, 11 A stage free, 12 scales ready.
+constexpr int kTraceRow = 1024;
+constexpr int kTraceRows = 13;
+__device__ __forceinline__ void trace_put(const GemmParams &P, int row, uint32_t i) {
+    if (P.trace != nullptr && blockIdx.x == 0 && i < (uint32_t)kTraceRow) {
+        uint32_t c;
+        asm volatile("mov.u32 %0, %%clock;" : "=r"(c));
+        P.trace[row * kTraceRow + i] = c;
+    }
+}
 
 // ------------------------------------------------------------------ helpers ----
 
@@ -102,8 +129,27 @@ __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, i
         "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
         : "memory");
 }
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int c0, int c1, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(map), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+        : "memory");
+}
+// Four rows (r0..r3) of 64 columns starting at column c of a 2D map, one row high box.
+__device__ __forceinline__ void tma_gather4(void *dst, const CUtensorMap *map, int c, int r0, int r1, int r2, int r3,
+                                            uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+        "%4, %5, %6}], [%7];" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(c), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(smem_u32(bar))
+        : "memory");
+}
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_n(uint64_t *bar, uint32_t n) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(n) : "memory");
 }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -119,6 +165,23 @@ __device__ __forceinline__ void tc_mma(uint32_t tmem, uint64_t ad, uint64_t bd, 
         "l"(ad), "l"(bd), "r"(idesc), "r"(acc)
         : "memory");
 }
+// D[tmem] (+)= A[tmem] * B[smem desc]^T; A: lane = row, column = a bf16 pair along K.
+__device__ __forceinline__ void tc_mma_ts(uint32_t d, uint32_t a, uint64_t bd, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+        "r"(a), "l"(bd), "r"(idesc), "r"(acc)
+        : "memory");
+}
+__device__ __forceinline__ void tc_st16(uint32_t taddr, const uint32_t *v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tc_ld8(uint32_t taddr, uint32_t *r) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
@@ -126,13 +189,6 @@ __device__ __forceinline__ void tc_ld8(uint32_t taddr, uint32_t *r) {
                  : "memory");
 }
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 __device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b) {
     uint32_t r;
@@ -156,6 +212,37 @@ __device__ __forceinline__ uint32_t split_pair(float a, float b, bool lo) {
     return pack_bf16x2(a - __uint_as_float(h << 16), b - __uint_as_float(h & 0xFFFF0000u));
 }
 
+
+// ------------------------------------------------------------ geometry ----
+
+struct StepGeo {
+    int kb;      // steps per pass of one item (K / 64 / ksplit)
+    int sps;     // q formats: steps per raw slot
+    int nslot;   // bf16: raw slots per step
+    int wpk;     // q formats: words per row per step
+    int rowb;    // q formats: bytes per row in a slot
+    int rawm;    // q formats: bytes per matrix in a slot
+};
+
+__host__ __device__ __forceinline__ StepGeo step_geo(int fmt, int n_mat, int K, int ksplit) {
+    StepGeo g;
+    g.kb = K / 64 / ksplit;
+    if (fmt == kAFmtBf16) {
+        g.sps = 1;
+        g.nslot = 2 * n_mat;
+        g.wpk = 64;
+        g.rowb = 128;
+        g.rawm = kGemmSlot / n_mat;
+    } else {
+        g.wpk = fmt == kAFmtQ4 ? 8 : 4;
+        g.sps = 1;
+        g.nslot = 1;
+        g.rowb = g.wpk * 4 * g.sps;
+        g.rawm = 128 * g.rowb;
+    }
+    return g;
+}
+
 // ----------------------------------------------------------- work items ----
 
 struct GemmTables {
@@ -165,7 +252,7 @@ struct GemmTables {
 };
 
 struct GemmItem {
-    int p, g, mt, c0, n, pos0;
+    int p, g, mt, sp, n, pos0;
 };
 
 __device__ __forceinline__ int gemm_group_count(const GemmProblem &pr, int g) {
@@ -173,15 +260,15 @@ __device__ __forceinline__ int gemm_group_count(const GemmProblem &pr, int g) {
 }
 
 // One warp per problem: prefix sums over groups of positions and of items.
-__device__ __forceinline__ void gemm_build_tables(const GemmParams &P, GemmTables *T, int warp, int lane) {
-    if (warp < P.n_prob) {
-        const GemmProblem &pr = P.prob[warp];
+__device__ __forceinline__ void gemm_build_tables(const GemmParams &P, GemmTables *T, int prob, int lane) {
+    if (prob < P.n_prob) {
+        const GemmProblem &pr = P.prob[prob];
         int c[8], it[8], sc = 0, si = 0;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const int g = 8 * lane + j;
             c[j] = g < pr.n_groups ? gemm_group_count(pr, g) : 0;
-            it[j] = (c[j] + kGemmNChunk - 1) / kGemmNChunk * pr.m_tiles;
+            it[j] = (c[j] + kGemmNChunk - 1) / kGemmNChunk * pr.m_tiles * pr.ksplit;
             sc += c[j];
             si += it[j];
         }
@@ -194,18 +281,20 @@ __device__ __forceinline__ void gemm_build_tables(const GemmParams &P, GemmTable
         int pc = xc - sc, pi = xi - si;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            T->goff[warp][8 * lane + j] = pc;
-            T->ipre[warp][8 * lane + j] = pi;
+            T->goff[prob][8 * lane + j] = pc;
+            T->ipre[prob][8 * lane + j] = pi;
             pc += c[j];
             pi += it[j];
         }
         if (lane == 31) {
-            T->goff[warp][kGemmMaxGroups] = pc;
-            T->ipre[warp][kGemmMaxGroups] = pi;
+            T->goff[prob][kGemmMaxGroups] = pc;
+            T->ipre[prob][kGemmMaxGroups] = pi;
         }
     }
 }
 
+// Items of a group in the order (m tile, K slice, token chunk): consecutive items share
+// the weight tile, so the CTAs working on the chunks of one expert read it from L2.
 __device__ __forceinline__ GemmItem gemm_item(const GemmParams &P, const GemmTables *T, int it) {
     GemmItem w;
     w.p = it >= T->total[1] ? 1 : 0;
@@ -221,34 +310,119 @@ __device__ __forceinline__ GemmItem gemm_item(const GemmParams &P, const GemmTab
     const GemmProblem &pr = P.prob[w.p];
     const int cnt = gemm_group_count(pr, w.g);
     const int chunks = (cnt + kGemmNChunk - 1) / kGemmNChunk;
-    w.mt = li / chunks;
-    const int ch = li - w.mt * chunks;
-    w.c0 = ch * kGemmNChunk;
-    w.n = min(kGemmNChunk, cnt - w.c0);
-    w.pos0 = T->goff[w.p][w.g] + w.c0;
+    const int per_mt = chunks * pr.ksplit;
+    w.mt = li / per_mt;
+    li -= w.mt * per_mt;
+    w.sp = li / chunks;
+    const int c0 = (li - w.sp * chunks) * kGemmNChunk;
+    w.n = min(kGemmNChunk, cnt - c0);
+    w.pos0 = T->goff[w.p][w.g] + c0;
     return w;
 }
 
-__device__ __forceinline__ int gemm_steps(const GemmProblem &pr) {
-    return __popc(pr.passes) * (pr.K / 64);
-}
-// pass of step s: the (s / kb)-th set bit of passes
-__device__ __forceinline__ int gemm_pass(const GemmProblem &pr, int s) {
-    int q = s / (pr.K / 64);
-    uint32_t b = (uint32_t)pr.passes;
+// pass of pass index q: the q-th set bit of passes (0: hi.hi  1: hi.lo  2: lo.hi)
+__device__ __forceinline__ int gemm_pass(int passes, int q) {
+    uint32_t b = (uint32_t)passes;
     while (q-- > 0) b &= b - 1;
-    return __ffs(b) - 1;   // 0: hi.hi  1: hi.lo  2: lo.hi
+    return __ffs(b) - 1;
 }
 
-__host__ __device__ __forceinline__ int raw_mat_bytes(int fmt) {
-    return fmt == kAFmtQ4 ? 4096 : fmt == kAFmtQ2 ? 2048 : 16384;
+// ------------------------------------------------------------- dequant ----
+// One thread converts row r, columns [32h, 32h+32) of a 64-column step (four groups of
+// 8) and stores them as 16 bf16 pairs into its TMEM lane (tcgen05.st, 16 columns), each
+// group as (v0,v4)(v1,v5)(v2,v6)(v3,v7): the K order [0,4,1,5,2,6,3,7].
+
+// gw[g]: group g's 8 values, value i at bit sh*i and value i+4 at bit sh*i + 16.
+template <int kFmt>
+__device__ __forceinline__ void dq_load(const uint8_t *raw, int h, uint32_t *gw) {
+    if (kFmt == kAFmtQ4) {
+        const uint4 v = lds128(raw + h * 16);
+        gw[0] = v.x; gw[1] = v.y; gw[2] = v.z; gw[3] = v.w;
+    } else {
+        const uint2 v = *reinterpret_cast<const uint2 *>(raw + h * 8);
+        const uint32_t g0 = v.x & 0xFFFFu, g1 = v.x >> 16, g2 = v.y & 0xFFFFu, g3 = v.y >> 16;
+        gw[0] = g0 | (g0 << 8); gw[1] = g1 | (g1 << 8);
+        gw[2] = g2 | (g2 << 8); gw[3] = g3 | (g3 << 8);
+    }
+}
+
+// taddr: this thread's lane, column of matrix 0's half h; matrix m at +32 m.
+template <int kFmt, int kNMat>
+__device__ __forceinline__ void dq_step_q(const uint8_t *raw, int rawm, const uint8_t *sc, int sidx, uint32_t taddr,
+                                          int h) {
+    constexpr int sh = kFmt == kAFmtQ4 ? 4 : 2;
+    constexpr uint32_t mask = kFmt == kAFmtQ4 ? 0x000F000Fu : 0x00030003u;
+    uint32_t gw[kNMat][4], s2[kNMat], b2[kNMat];
+#pragma unroll
+    for (int m = 0; m < kNMat; ++m) {
+        dq_load<kFmt>(raw + m * rawm, h, gw[m]);
+        const uint32_t s16 = reinterpret_cast<const uint16_t *>(sc + m * kGemmScStage)[sidx];
+        const uint32_t b16 = reinterpret_cast<const uint16_t *>(sc + m * kGemmScStage + 2048)[sidx];
+        s2[m] = s16 | (s16 << 16);
+        b2[m] = b16 | (b16 << 16);
+    }
+#pragma unroll
+    for (int m = 0; m < kNMat; ++m) {
+        uint32_t o[16];
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t qq = ((gw[m][jj] >> (sh * i)) & mask) | 0x43004300u;
+                o[4 * jj + i] = bf16x2_fma(bf16x2_sub(qq, 0x43004300u), s2[m], b2[m]);
+            }
+        tc_st16(taddr + 32 * m, o);
+    }
+}
+
+// fp32-exact planes (router): hi = bf16(q*s + b), lo = bf16(q*s + b - hi).
+template <int kFmt>
+__device__ __forceinline__ void dq_step_split(const uint8_t *raw, const uint8_t *sc, int sidx, uint32_t taddr, int h,
+                                              bool lo) {
+    constexpr int sh = kFmt == kAFmtQ4 ? 4 : 2;
+    constexpr uint32_t mask = kFmt == kAFmtQ4 ? 0x000F000Fu : 0x00030003u;
+    uint32_t gw[4];
+    dq_load<kFmt>(raw, h, gw);
+    const float sf = __uint_as_float((uint32_t)reinterpret_cast<const uint16_t *>(sc)[sidx] << 16);
+    const float bf = __uint_as_float((uint32_t)reinterpret_cast<const uint16_t *>(sc + 2048)[sidx] << 16);
+    uint32_t o[16];
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t qq = (gw[jj] >> (sh * i)) & mask;
+            o[4 * jj + i] = split_pair(fmaf((float)(qq & 0xFFFFu), sf, bf), fmaf((float)(qq >> 16), sf, bf), lo);
+        }
+    tc_st16(taddr, o);
+}
+
+// bf16 rows: the four words of a group are (v0,v1)(v2,v3)(v4,v5)(v6,v7).
+template <int kNMat>
+__device__ __forceinline__ void dq_step_bf16(const uint8_t *raw, int rawm, uint32_t taddr, bool zero) {
+    uint4 v[kNMat][4];
+#pragma unroll
+    for (int m = 0; m < kNMat; ++m)
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) v[m][jj] = lds128(raw + m * rawm + jj * 16);
+#pragma unroll
+    for (int m = 0; m < kNMat; ++m) {
+        uint32_t o[16];
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+            o[4 * jj + 0] = zero ? 0u : prmt(v[m][jj].x, v[m][jj].z, 0x5410);
+            o[4 * jj + 1] = zero ? 0u : prmt(v[m][jj].x, v[m][jj].z, 0x7632);
+            o[4 * jj + 2] = zero ? 0u : prmt(v[m][jj].y, v[m][jj].w, 0x5410);
+            o[4 * jj + 3] = zero ? 0u : prmt(v[m][jj].y, v[m][jj].w, 0x7632);
+        }
+        tc_st16(taddr + 32 * m, o);
+    }
 }
 
 // ------------------------------------------------------------------ kernel ----
 
 struct GemmSmem {
-    uint64_t raw_full[8], raw_empty[8];
-    uint64_t sc_full[kGemmSS], sc_empty[kGemmSS];
+    uint64_t raw_full[kGemmMaxSlots], raw_empty[kGemmMaxSlots];
+    uint64_t sc_full[2 * kGemmSS], sc_empty[2 * kGemmSS];   // [group][stage]
     uint64_t a_full[kGemmSA], a_empty[kGemmSA];
     uint64_t b_full[kGemmSB], b_empty[kGemmSB];
     uint64_t acc_full[2], acc_empty[2];
@@ -258,13 +432,38 @@ struct GemmSmem {
     GemmTables T;
 };
 
+__host__ __device__ constexpr size_t gemm_smem_bytes(int sr) {
+    return 1024 + (size_t)kGemmSB * kGemmBStage + (size_t)2 * kGemmSS * 2 * kGemmScStage +
+           (size_t)sr * kGemmSlot + sizeof(GemmSmem);
+}
+
+// Position in a ring of mbarrier-guarded stages: index, phase parity, total advances.
+struct Ring {
+    uint32_t idx = 0, phase = 0, count = 0, n;
+    __device__ explicit Ring(int n_) : n((uint32_t)n_) {}
+    __device__ __forceinline__ void next() {
+        ++count;
+        if (++idx == n) { idx = 0; phase ^= 1; }
+    }
+    // wait (bounded) for the last fill of every stage to complete
+    __device__ void drain(uint64_t *full, uint64_t deadline) const {
+        const uint32_t k = count < n ? count : n;
+        for (uint32_t i = 0; i < k; ++i) {
+            const uint32_t back = i + 1;   // the back-th most recent fill
+            const uint32_t st = (idx + n - back % n) % n;
+            const uint32_t ph = back > idx ? phase ^ 1 : phase;
+            if (!mbar_wait_sleep(&full[st], ph, deadline)) return;
+        }
+    }
+};
+
 __device__ __forceinline__ void gemm_fail(GemmSmem *S, int *err) {
     S->abort = 1;
     atomicCAS(err, 0, kErrTimeout);
 }
 
-// K-permuted slot order within an 8-column group: slot s holds column kPermCol[s].
-__device__ __forceinline__ int kperm_pos(int col) {   // position of column col (within its group of 8)
+// Position of column `col` inside its 8-column group in the K order [0,4,1,5,2,6,3,7].
+__host__ __device__ __forceinline__ int kperm_pos(int col) {
     const int j = col & 7;
     return (col & ~7) | (j < 4 ? 2 * j : 2 * (j - 4) + 1);
 }
@@ -272,20 +471,20 @@ __device__ __forceinline__ int kperm_pos(int col) {   // position of column col 
 __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_constant__ GemmParams P) {
     extern __shared__ __align__(1024) uint8_t smraw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
-    uint8_t *sA = sm;                                  // kGemmSA x 2 x 16 KB
-    uint8_t *sB = sA + kGemmSA * 2 * kGemmAStage;      // kGemmSB x 16 KB
-    uint8_t *sSc = sB + kGemmSB * kGemmBStage;         // kGemmSS x 2 x 4 KB
-    uint8_t *sRaw = sSc + kGemmSS * 2 * kGemmScStage;  // sr x raw_stage
-    GemmSmem *S = reinterpret_cast<GemmSmem *>(sRaw + P.sr * P.raw_stage);
+    uint8_t *sB = sm;                                  // kGemmSB x 16 KB
+    uint8_t *sSc = sB + kGemmSB * kGemmBStage;         // 2 groups x kGemmSS x 2 x 4 KB
+    uint8_t *sRaw = sSc + 2 * kGemmSS * 2 * kGemmScStage;  // sr x 8 KB
+    GemmSmem *S = reinterpret_cast<GemmSmem *>(sRaw + P.sr * kGemmSlot);
+    const int SR = P.sr;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint64_t deadline = globaltimer_ns() + P.timeout_ns;
 
     if (tid == 0) {
-        for (int i = 0; i < P.sr; ++i) { mbar_init(&S->raw_full[i], 1); mbar_init(&S->raw_empty[i], 8); }
-        for (int i = 0; i < kGemmSS; ++i) { mbar_init(&S->sc_full[i], 1); mbar_init(&S->sc_empty[i], 8); }
-        for (int i = 0; i < kGemmSA; ++i) { mbar_init(&S->a_full[i], 8); mbar_init(&S->a_empty[i], 1); }
-        for (int i = 0; i < kGemmSB; ++i) { mbar_init(&S->b_full[i], 64); mbar_init(&S->b_empty[i], 1); }
+        for (int i = 0; i < SR; ++i) { mbar_init(&S->raw_full[i], 1); mbar_init(&S->raw_empty[i], 4); }
+        for (int i = 0; i < 2 * kGemmSS; ++i) { mbar_init(&S->sc_full[i], 1); mbar_init(&S->sc_empty[i], 4); }
+        for (int i = 0; i < kGemmSA; ++i) { mbar_init(&S->a_full[i], 4); mbar_init(&S->a_empty[i], 1); }
+        for (int i = 0; i < kGemmSB; ++i) { mbar_init(&S->b_full[i], 1); mbar_init(&S->b_empty[i], 1); }
         for (int i = 0; i < 2; ++i) { mbar_init(&S->acc_full[i], 1); mbar_init(&S->acc_empty[i], 4); }
         mbar_init(&S->drain, 1);
         S->abort = 0;
@@ -295,7 +494,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(&S->tmem_base)));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
-    gemm_build_tables(P, &S->T, warp - 2 >= 0 ? warp - 2 : 99, lane);
+    gemm_build_tables(P, &S->T, warp >= 2 ? warp - 2 : kGemmMaxProblems, lane);
     __syncthreads();
     if (tid == 0) {
         S->T.total[0] = 0;
@@ -311,228 +510,244 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
     if (warp == 0) {
         // ------------------------------------------------ TMA producer ----
         if (lane == 0) {
-            uint32_t rit = 0, sit = 0;
-            for (int it = blockIdx.x; it < n_items && !S->abort; it += gridDim.x) {
+            Ring raw(SR), sc0(kGemmSS), sc1(kGemmSS);
+            uint32_t gstep = 0;   // steps issued so far: step parity picks the dequant group
+            bool ok = true;
+            for (int it = blockIdx.x; it < n_items && ok && !S->abort; it += gridDim.x) {
                 const GemmItem w = gemm_item(P, &S->T, it);
                 const GemmProblem &pr = P.prob[w.p];
+                const StepGeo G = step_geo(pr.fmt, pr.n_mat, pr.K, pr.ksplit);
                 const bool q = pr.fmt != kAFmtBf16;
-                const int kb = pr.K / 64, steps = gemm_steps(pr);
-                const int rawm = raw_mat_bytes(pr.fmt);
-                const int wpk = pr.fmt == kAFmtQ4 ? 8 : pr.fmt == kAFmtQ2 ? 4 : 64;
-                for (int s = 0; s < steps; ++s) {
-                    const int ks = s % kb;
-                    if (q && (ks & 7) == 0) {
-                        const int st = sit % kGemmSS;
-                        if (!mbar_wait(&S->sc_empty[st], ((sit / kGemmSS) & 1) ^ 1, deadline)) { gemm_fail(S, P.err); break; }
-                        mbar_arrive_expect_tx(&S->sc_full[st], pr.n_mat * kGemmScStage);
-                        for (int m = 0; m < pr.n_mat; ++m) {
-                            uint8_t *d = sSc + (st * 2 + m) * kGemmScStage;
-                            tma_load_4d(d, &pr.ts[m], ks, 0, w.mt * 8, w.g, &S->sc_full[st]);
-                            tma_load_4d(d + 2048, &pr.tb[m], ks, 0, w.mt * 8, w.g, &S->sc_full[st]);
+                const int npass = __popc(pr.passes), ks0 = w.sp * G.kb;
+                for (int ps = 0; ps < npass && ok; ++ps) {
+                    int lastw[2] = {-1, -1};   // scale window last loaded for each group
+                    for (int j = 0; j < G.kb; ++j, ++gstep) {
+                        const int ks = ks0 + j, grp = gstep & 1;
+                        if (q) {
+                            if ((ks >> 3) != lastw[grp]) {
+                                lastw[grp] = ks >> 3;
+                                Ring &sc = grp ? sc1 : sc0;
+                                const int si = grp * kGemmSS + sc.idx;
+                                if (!mbar_wait_sleep(&S->sc_empty[si], sc.phase ^ 1, deadline)) { ok = false; break; }
+                                mbar_arrive_expect_tx(&S->sc_full[si], pr.n_mat * kGemmScStage);
+                                for (int m = 0; m < pr.n_mat; ++m) {
+                                    uint8_t *d = sSc + (si * 2 + m) * kGemmScStage;
+                                    tma_load_4d(d, &pr.ts[m], ks & ~7, 0, w.mt * 8, w.g, &S->sc_full[si]);
+                                    tma_load_4d(d + 2048, &pr.tb[m], ks & ~7, 0, w.mt * 8, w.g, &S->sc_full[si]);
+                                }
+                                sc.next();
+                            }
+                            if (!mbar_wait_sleep(&S->raw_empty[raw.idx], raw.phase ^ 1, deadline)) { ok = false; break; }
+                            trace_put(P, 0, raw.count);
+                            mbar_arrive_expect_tx(&S->raw_full[raw.idx], pr.n_mat * G.rawm);
+                            for (int m = 0; m < pr.n_mat; ++m)
+                                tma_load_4d(sRaw + raw.idx * kGemmSlot + m * G.rawm, &pr.tw[m], ks * G.wpk, 0, w.mt * 8,
+                                            w.g, &S->raw_full[raw.idx]);
+                            raw.next();
+                        } else {
+                            const int bands = 8 / G.nslot;
+                            for (int qs = 0; qs < G.nslot; ++qs) {
+                                if (!mbar_wait_sleep(&S->raw_empty[raw.idx], raw.phase ^ 1, deadline)) { ok = false; break; }
+                                mbar_arrive_expect_tx(&S->raw_full[raw.idx], kGemmSlot);
+                                for (int m = 0; m < pr.n_mat; ++m)
+                                    tma_load_4d(sRaw + raw.idx * kGemmSlot + m * G.rawm, &pr.tw[m], ks * 64, 0,
+                                                w.mt * 8 + qs * bands, w.g, &S->raw_full[raw.idx]);
+                                raw.next();
+                            }
+                            if (!ok) break;
                         }
-                        ++sit;
                     }
-                    const int st = rit % P.sr;
-                    if (!mbar_wait(&S->raw_empty[st], ((rit / P.sr) & 1) ^ 1, deadline)) { gemm_fail(S, P.err); break; }
-                    mbar_arrive_expect_tx(&S->raw_full[st], pr.n_mat * rawm);
-                    for (int m = 0; m < pr.n_mat; ++m)
-                        tma_load_4d(sRaw + st * P.raw_stage + m * rawm, &pr.tw[m], ks * wpk, 0, w.mt * 8, w.g,
-                                    &S->raw_full[st]);
-                    ++rit;
                 }
             }
-            // drain: the last fill of every stage has landed before the CTA may exit
-            for (uint32_t j = rit > (uint32_t)P.sr ? rit - P.sr : 0; j < rit; ++j)
-                if (!mbar_wait(&S->raw_full[j % P.sr], (j / P.sr) & 1, deadline)) break;
-            for (uint32_t j = sit > (uint32_t)kGemmSS ? sit - kGemmSS : 0; j < sit; ++j)
-                if (!mbar_wait(&S->sc_full[j % kGemmSS], (j / kGemmSS) & 1, deadline)) break;
+            if (!ok) gemm_fail(S, P.err);
+            // drain: the last fill of every slot has landed before the CTA may exit
+            raw.drain(S->raw_full, deadline);
+            sc0.drain(S->sc_full, deadline);
+            sc1.drain(S->sc_full + kGemmSS, deadline);
         }
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer ----
         if (lane == 0) {
-            uint32_t ait = 0, bit = 0, tile = 0;
-            bool issued = false;
-            for (int it = blockIdx.x; it < n_items && !S->abort; it += gridDim.x, ++tile) {
+            Ring a(kGemmSA), b(kGemmSB);
+            uint32_t tile = 0;
+            bool issued = false, ok = true;
+            for (int it = blockIdx.x; it < n_items && ok && !S->abort; it += gridDim.x, ++tile) {
                 const GemmItem w = gemm_item(P, &S->T, it);
                 const GemmProblem &pr = P.prob[w.p];
-                const int steps = gemm_steps(pr);
-                const int ab = tile & 1;
-                if (!mbar_wait(&S->acc_empty[ab], ((tile >> 1) & 1) ^ 1, deadline)) { gemm_fail(S, P.err); break; }
+                const StepGeo G = step_geo(pr.fmt, pr.n_mat, pr.K, pr.ksplit);
+                const int steps = __popc(pr.passes) * G.kb;
+                const int ab = tile % P.acc_bufs;
+                if (!mbar_wait_sleep(&S->acc_empty[ab], ((tile / P.acc_bufs) & 1) ^ 1, deadline)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t idesc = idesc_bf16((w.n + 15) & ~15);
-                bool ok = true;
+                const uint32_t d0 = tmem + ab * 128;   // accumulator, matrix 0
                 for (int s = 0; s < steps; ++s) {
-                    const int sa = ait % kGemmSA, sb = bit % kGemmSB;
-                    if (!mbar_wait(&S->a_full[sa], (ait / kGemmSA) & 1, deadline) ||
-                        !mbar_wait(&S->b_full[sb], (bit / kGemmSB) & 1, deadline)) {
-                        ok = false;
-                        break;
-                    }
+                    if (!mbar_wait_sleep(&S->b_full[b.idx], b.phase, deadline)) { ok = false; break; }
+                    trace_put(P, 8, a.count);
+                    if (!mbar_wait_sleep(&S->a_full[a.idx], a.phase, deadline)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t bsa = smem_u32(sB + sb * kGemmBStage);
-                    for (int kk = 0; kk < 4; ++kk)
-                        for (int m = 0; m < pr.n_mat; ++m)
-                            tc_mma(tmem + ab * 256 + m * 128, sw128_desc(smem_u32(sA + (sa * 2 + m) * kGemmAStage)) + 2 * kk,
-                                   sw128_desc(bsa) + 2 * kk, idesc, (s | kk) ? 1u : 0u);
+                    trace_put(P, 4, a.count);
+                    const uint64_t bd = sw128_desc(smem_u32(sB + b.idx * kGemmBStage));
+                    const uint32_t a0 = tmem + kGemmAccCols + a.idx * kGemmACols;   // A stage, matrix 0
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        tc_mma_ts(d0, a0 + 8 * kk, bd + 2 * kk, idesc, (s | kk) ? 1u : 0u);
+                        if (pr.n_mat == 2) tc_mma_ts(d0 + 128, a0 + 32 + 8 * kk, bd + 2 * kk, idesc, (s | kk) ? 1u : 0u);
+                    }
                     issued = true;
-                    tc_commit(&S->a_empty[sa]);
-                    tc_commit(&S->b_empty[sb]);
-                    ++ait;
-                    ++bit;
+                    tc_commit(&S->a_empty[a.idx]);
+                    tc_commit(&S->b_empty[b.idx]);
+                    a.next();
+                    b.next();
                 }
-                if (!ok) { gemm_fail(S, P.err); break; }
+                if (!ok) break;
                 tc_commit(&S->acc_full[ab]);
             }
+            if (!ok) gemm_fail(S, P.err);
             if (issued) {   // every MMA issued has completed before TMEM is freed
                 tc_commit(&S->drain);
-                mbar_wait(&S->drain, 0, deadline + 100000000ull);
+                mbar_wait_sleep(&S->drain, 0, deadline + 100000000ull);
             }
         }
-    } else if (warp < 4) {
-        // ------------------------------------------------ B loader (64 threads) ----
-        const int lt = tid - 64;
-        uint32_t bit = 0;
-        uint32_t pending = 0;   // committed groups not yet signalled (0 or 1)
-        bool ok = true;
-        for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
-            const GemmItem w = gemm_item(P, &S->T, it);
-            const GemmProblem &pr = P.prob[w.p];
-            const int kb = pr.K / 64, steps = gemm_steps(pr);
-            const int n16 = (w.n + 15) & ~15;
-            for (int s = 0; s < steps; ++s) {
-                const int st = bit % kGemmSB;
-                const bool wait_ok = __all_sync(0xffffffffu, mbar_wait(&S->b_empty[st], ((bit / kGemmSB) & 1) ^ 1, deadline));
-                if (!wait_ok || S->abort) { ok = false; break; }
-                const int pass = gemm_pass(pr, s), ks = s % kb;
-                const uint16_t *src = pass == 1 ? pr.b_lo : pr.b_hi;
-                uint8_t *dst = sB + st * kGemmBStage;
-                for (int c = lt; c < n16 * 8; c += 64) {
-                    const int r = c >> 3, ch = c & 7;
-                    if (r < w.n) {
-                        const int p = pr.in_base + w.pos0 + r;
-                        const int row = pr.perm ? pr.perm[p] : p;
-                        cp_async16(dst + sw128_off(r, ch), src + (size_t)row * pr.K + ks * 64 + ch * 8);
+    } else if (warp == 2) {
+        // ------------------------------------------------ B loader (TMA, 16-row tiles) ----
+        if (lane == 0) {
+            Ring b(kGemmSB);
+            bool ok = true;
+            for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+                const GemmItem w = gemm_item(P, &S->T, it);
+                const GemmProblem &pr = P.prob[w.p];
+                const StepGeo G = step_geo(pr.fmt, pr.n_mat, pr.K, pr.ksplit);
+                const int npass = __popc(pr.passes), ks0 = w.sp * G.kb;
+                const int nt = (w.n + 15) >> 4, row0 = pr.in_base + w.pos0;
+                for (int ps = 0; ps < npass && ok; ++ps) {
+                    const CUtensorMap *map = &pr.tx[gemm_pass(pr.passes, ps) == 1 ? 1 : 0];
+                    for (int j = 0; j < G.kb; ++j) {
+                        if (!mbar_wait_sleep(&S->b_empty[b.idx], b.phase ^ 1, deadline) || S->abort) { ok = false; break; }
+                        uint8_t *dst = sB + b.idx * kGemmBStage;
+                        trace_put(P, 1, b.count);
+                        mbar_arrive_expect_tx(&S->b_full[b.idx], nt * 2048);
+                        for (int i = 0; i < nt; ++i)
+                            tma_load_2d(dst + i * 2048, map, (ks0 + j) * 64, row0 + 16 * i, &S->b_full[b.idx]);
+                        b.next();
                     }
                 }
-                cp_async_commit();
-                if (pending) {   // the previous stage is complete: publish it
-                    cp_async_wait<1>();
-                    fence_async_smem();
-                    mbar_arrive(&S->b_full[(bit - 1) % kGemmSB]);
+            }
+            if (!ok) gemm_fail(S, P.err);
+            b.drain(S->b_full, deadline);
+        }
+    } else if (warp == 3) {
+        // diagnostics only: with tracing on, record when each raw slot's data lands
+        if (P.trace != nullptr && blockIdx.x == 0 && lane == 0) {
+            Ring raw(SR);
+            for (int it = blockIdx.x; it < n_items && !S->abort; it += gridDim.x) {
+                const GemmItem w = gemm_item(P, &S->T, it);
+                const GemmProblem &pr = P.prob[w.p];
+                const StepGeo G = step_geo(pr.fmt, pr.n_mat, pr.K, pr.ksplit);
+                const int steps = __popc(pr.passes) * G.kb;
+                const int slots = pr.fmt != kAFmtBf16 ? steps / G.sps : steps * G.nslot;
+                for (int q = 0; q < slots; ++q) {
+                    if (!mbar_wait_sleep(&S->raw_full[raw.idx], raw.phase, deadline)) break;
+                    trace_put(P, 7, raw.count);
+                    raw.next();
                 }
-                pending = 1;
-                ++bit;
             }
         }
-        cp_async_wait<0>();
-        if (pending && ok) {
-            fence_async_smem();
-            mbar_arrive(&S->b_full[(bit - 1) % kGemmSB]);
-        }
-        if (!ok) gemm_fail(S, P.err);
     } else if (warp < 12) {
-        // ------------------------------------------------ dequant (256 threads) ----
-        const int dt = tid - 128, r = dt & 127, h = dt >> 7;
-        uint32_t rit = 0, sit = 0, ait = 0;
+        // ------------------------------------------------ dequant (2 x 128 threads) ----
+        // Two groups of four warps take alternate steps, so one group's barrier waits
+        // overlap the other's conversion. A thread converts one full row of a step.
+        const int grp = (warp - 4) >> 2, r = 32 * (warp & 3) + lane;
+        const uint32_t tlane = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + kGemmAccCols;
+        Ring raw(SR), sc(kGemmSS), a(kGemmSA);
+        uint32_t gstep = 0;
         bool ok = true;
         for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
             const GemmItem w = gemm_item(P, &S->T, it);
             const GemmProblem &pr = P.prob[w.p];
+            const StepGeo G = step_geo(pr.fmt, pr.n_mat, pr.K, pr.ksplit);
             const bool q = pr.fmt != kAFmtBf16;
-            const int kb = pr.K / 64, steps = gemm_steps(pr);
-            const int rawm = raw_mat_bytes(pr.fmt);
-            for (int s = 0; s < steps; ++s) {
-                const int ks = s % kb;
-                const int lo = gemm_pass(pr, s) == 2;
-                const int ss = sit % kGemmSS;
-                if (q && (ks & 7) == 0)
-                    if (!mbar_wait_warp(&S->sc_full[ss], (sit / kGemmSS) & 1, deadline)) { ok = false; break; }
-                const int sr = rit % P.sr, sa = ait % kGemmSA;
-                if (!mbar_wait_warp(&S->raw_full[sr], (rit / P.sr) & 1, deadline) ||
-                    !mbar_wait_warp(&S->a_empty[sa], ((ait / kGemmSA) & 1) ^ 1, deadline)) {
-                    ok = false;
-                    break;
-                }
-                if (S->abort) { ok = false; break; }
-                for (int m = 0; m < pr.n_mat; ++m) {
-                    const uint8_t *raw = sRaw + sr * P.raw_stage + m * rawm;
-                    uint8_t *a = sA + (sa * 2 + m) * kGemmAStage + r * 128;
-                    const int rx = r & 7;
-                    if (!q) {
-                        // bf16 rows: 4 groups of 8 columns, pair (v_j, v_{j+4}) per word
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            const uint4 v = lds128(raw + r * 128 + h * 64 + j * 16);
-                            uint4 o;
-                            if (pr.split && lo) {
-                                o = make_uint4(0, 0, 0, 0);
-                            } else {
-                                o.x = prmt(v.x, v.z, 0x5410);
-                                o.y = prmt(v.x, v.z, 0x7632);
-                                o.z = prmt(v.y, v.w, 0x5410);
-                                o.w = prmt(v.y, v.w, 0x7632);
-                            }
-                            *reinterpret_cast<uint4 *>(a + (((4 * h + j) ^ rx) << 4)) = o;
-                        }
+            const int npass = __popc(pr.passes), ks0 = w.sp * G.kb;
+            const int rps = 128 / G.nslot, qs = r / rps;   // bf16: slot holding this row
+            for (int ps = 0; ps < npass && ok; ++ps) {
+                const bool lo = gemm_pass(pr.passes, ps) == 2;
+                int lastw = -1;
+                for (int j = 0; j < G.kb; ++j, ++gstep) {
+                    const int ks = ks0 + j;
+                    if ((int)(gstep & 1) != grp) {   // the other group's step: advance the rings
+                        for (int k = 0; k < G.nslot; ++k) raw.next();
+                        a.next();
                         continue;
                     }
-                    const uint8_t *sc = sSc + (ss * 2 + m) * kGemmScStage;
-                    const uint16_t s16 = reinterpret_cast<const uint16_t *>(sc)[r * 8 + (ks & 7)];
-                    const uint16_t b16 = reinterpret_cast<const uint16_t *>(sc + 2048)[r * 8 + (ks & 7)];
-                    // 4 words of 8 q4 values, or 2 words of 16 q2 values: 4 groups of 8
-                    uint32_t gw[4];   // per group: values at bits [0,16) (q4: 8 x 4 bits)
-                    int sh = 4;       // bit step between consecutive values of a group
-                    if (pr.fmt == kAFmtQ4) {
-                        const uint4 v = lds128(raw + r * 32 + h * 16);
-                        gw[0] = v.x; gw[1] = v.y; gw[2] = v.z; gw[3] = v.w;
-                    } else {
-                        const uint2 v = *reinterpret_cast<const uint2 *>(raw + r * 16 + h * 8);
-                        // 8 q2 values of a group in bits [0,16): spread so (v_i, v_{i+4}) sit 16 apart
-                        const uint32_t g0 = v.x & 0xFFFFu, g1 = v.x >> 16, g2 = v.y & 0xFFFFu, g3 = v.y >> 16;
-                        gw[0] = g0 | (g0 << 8); gw[1] = g1 | (g1 << 8);
-                        gw[2] = g2 | (g2 << 8); gw[3] = g3 | (g3 << 8);
-                        sh = 2;
-                    }
-                    const uint32_t mask = pr.fmt == kAFmtQ4 ? 0x000F000Fu : 0x00030003u;
-                    if (!pr.split) {
-                        const uint32_t s2 = (uint32_t)s16 | ((uint32_t)s16 << 16);
-                        const uint32_t b2 = (uint32_t)b16 | ((uint32_t)b16 << 16);
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            uint32_t o[4];
-#pragma unroll
-                            for (int i = 0; i < 4; ++i) {
-                                const uint32_t qq = ((gw[j] >> (sh * i)) & mask) | 0x43004300u;
-                                o[i] = bf16x2_fma(bf16x2_sub(qq, 0x43004300u), s2, b2);
-                            }
-                            *reinterpret_cast<uint4 *>(a + (((4 * h + j) ^ rx) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+                    if (lane == 0 && warp == 4) trace_put(P, 10, a.count);
+                    if (!__all_sync(0xffffffffu, mbar_wait_sleep(&S->a_empty[a.idx], a.phase ^ 1, deadline))) { ok = false; break; }
+                    tc_fence_after();
+                    if (lane == 0 && warp == 4) trace_put(P, 11, a.count);
+                    const uint32_t ta = tlane + a.idx * kGemmACols;
+                    if (!q) {
+                        const uint32_t slot = raw.idx + qs < (uint32_t)SR ? raw.idx + qs : raw.idx + qs - SR;
+                        const uint32_t ph = raw.idx + qs < (uint32_t)SR ? raw.phase : raw.phase ^ 1;
+                        if (!__all_sync(0xffffffffu, mbar_wait_sleep(&S->raw_full[slot], ph, deadline))) { ok = false; break; }
+                        const uint8_t *src = sRaw + slot * kGemmSlot + (r - qs * rps) * 128;
+                        if (pr.n_mat == 2) {
+                            dq_step_bf16<2>(src, G.rawm, ta, pr.split && lo);
+                            dq_step_bf16<2>(src + 64, G.rawm, ta + 16, pr.split && lo);
+                        } else {
+                            dq_step_bf16<1>(src, G.rawm, ta, pr.split && lo);
+                            dq_step_bf16<1>(src + 64, G.rawm, ta + 16, pr.split && lo);
                         }
-                    } else {
-                        const float sf = __uint_as_float((uint32_t)s16 << 16), bf = __uint_as_float((uint32_t)b16 << 16);
+                        tc_wait_st();
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) {
+                            mbar_arrive_n(&S->raw_empty[slot], 4 * 32 / rps);   // 4 arrivals per slot
+                            mbar_arrive(&S->a_full[a.idx]);
+                        }
+                        for (int k = 0; k < G.nslot; ++k) raw.next();
+                        a.next();
+                        continue;
+                    }
+                    const int si = grp * kGemmSS + sc.idx;
+                    const bool new_window = (ks >> 3) != lastw;
+                    if (new_window) {
+                        lastw = ks >> 3;
+                        if (!__all_sync(0xffffffffu, mbar_wait_sleep(&S->sc_full[si], sc.phase, deadline))) { ok = false; break; }
+                    }
+                    if (!__all_sync(0xffffffffu, mbar_wait_sleep(&S->raw_full[raw.idx], raw.phase, deadline))) { ok = false; break; }
+                    if (lane == 0 && warp == 4) trace_put(P, 2, a.count);
+                    {
+                        const uint8_t *src = sRaw + raw.idx * kGemmSlot + r * G.rowb;
+                        const uint8_t *scp = sSc + si * 2 * kGemmScStage;
+                        const int sidx = r * 8 + (ks & 7);
 #pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            uint32_t o[4];
-#pragma unroll
-                            for (int i = 0; i < 4; ++i) {
-                                const uint32_t qq = (gw[j] >> (sh * i)) & mask;
-                                const float va = fmaf((float)(qq & 0xFFFFu), sf, bf);
-                                const float vb = fmaf((float)(qq >> 16), sf, bf);
-                                o[i] = split_pair(va, vb, lo);
+                        for (int hh = 0; hh < 2; ++hh) {
+                            if (pr.fmt == kAFmtQ4) {
+                                if (pr.split) dq_step_split<kAFmtQ4>(src, scp, sidx, ta + 16 * hh, hh, lo);
+                                else if (pr.n_mat == 2) dq_step_q<kAFmtQ4, 2>(src, G.rawm, scp, sidx, ta + 16 * hh, hh);
+                                else dq_step_q<kAFmtQ4, 1>(src, G.rawm, scp, sidx, ta + 16 * hh, hh);
+                            } else {
+                                if (pr.split) dq_step_split<kAFmtQ2>(src, scp, sidx, ta + 16 * hh, hh, lo);
+                                else if (pr.n_mat == 2) dq_step_q<kAFmtQ2, 2>(src, G.rawm, scp, sidx, ta + 16 * hh, hh);
+                                else dq_step_q<kAFmtQ2, 1>(src, G.rawm, scp, sidx, ta + 16 * hh, hh);
                             }
-                            *reinterpret_cast<uint4 *>(a + (((4 * h + j) ^ rx) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
                         }
                     }
+                    tc_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    // last step of this group in the scale window: the next one is 2 steps on
+                    const bool rel_sc = ((ks + 2) >> 3) != (ks >> 3) || j + 2 >= G.kb;
+                    if (lane == 0 && warp == 4) trace_put(P, 3, a.count);
+                    if (lane == 0 && warp == 11) trace_put(P, 9, a.count);
+                    if (lane == 0) {
+                        mbar_arrive(&S->a_full[a.idx]);
+                        mbar_arrive(&S->raw_empty[raw.idx]);
+                        if (rel_sc) mbar_arrive(&S->sc_empty[si]);
+                    }
+                    if (rel_sc) { sc.next(); lastw = -1; }
+                    raw.next();
+                    a.next();
                 }
-                fence_async_smem();
-                __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(&S->raw_empty[sr]);
-                    mbar_arrive(&S->a_full[sa]);
-                    if (q && ((ks & 7) == 7 || ks == kb - 1)) mbar_arrive(&S->sc_empty[ss]);
-                }
-                if (q && ((ks & 7) == 7 || ks == kb - 1)) ++sit;
-                ++rit;
-                ++ait;
             }
         }
         if (!ok && lane == 0) gemm_fail(S, P.err);
@@ -543,16 +758,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
         for (int it = blockIdx.x; it < n_items; it += gridDim.x, ++tile) {
             const GemmItem w = gemm_item(P, &S->T, it);
             const GemmProblem &pr = P.prob[w.p];
-            const int ab = tile & 1;
-            const bool ok = mbar_wait_warp(&S->acc_full[ab], (tile >> 1) & 1, deadline);
+            const int ab = tile % P.acc_bufs;
+            const bool ok = __all_sync(0xffffffffu, mbar_wait_sleep(&S->acc_full[ab], (tile / P.acc_bufs) & 1, deadline));
             if (!ok || S->abort) {
                 if (!ok && lane == 0) gemm_fail(S, P.err);
                 break;
             }
             tc_fence_after();
+            if (tid == 384) trace_put(P, 5, tile);
             const int m = w.mt * 128 + row;
-            const uint32_t tbase = tmem + ((uint32_t)(32 * eq) << 16) + ab * 256;
-            const int obase = pr.out_base + w.pos0;
+            const uint32_t tbase = tmem + ((uint32_t)(32 * eq) << 16) + ab * 128;
+            const int obase = pr.out_base + w.sp * pr.split_rows + w.pos0;
             for (int c0 = 0; c0 < w.n; c0 += 8) {
                 uint32_t g[8], u[8];
                 tc_ld8(tbase + c0, g);
@@ -563,28 +779,33 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
                     uint16_t *o = static_cast<uint16_t *>(pr.out);
                     const int col = kperm_pos(m);
 #pragma unroll
-                    for (int j = 0; j < 8; ++j)
-                        if (j < nc) {
-                            const float gv = __uint_as_float(g[j]), uv = __uint_as_float(u[j]);
+                    for (int jj = 0; jj < 8; ++jj)
+                        if (jj < nc) {
+                            const float gv = __uint_as_float(g[jj]), uv = __uint_as_float(u[jj]);
                             const float a = gv / (1.f + expf(-gv)) * uv;
-                            o[(size_t)(obase + c0 + j) * pr.ld_out + col] = (uint16_t)(pack_bf16x2(a, 0.f) & 0xFFFFu);
+                            o[(size_t)(obase + c0 + jj) * pr.ld_out + col] = (uint16_t)(pack_bf16x2(a, 0.f) & 0xFFFFu);
                         }
                 } else if (pr.epi == kEpiBf16) {
                     uint16_t *o = static_cast<uint16_t *>(pr.out);
 #pragma unroll
-                    for (int j = 0; j < 8; ++j)
-                        if (j < nc)
-                            o[(size_t)(obase + c0 + j) * pr.ld_out + m] =
-                                (uint16_t)(pack_bf16x2(__uint_as_float(g[j]), 0.f) & 0xFFFFu);
+                    for (int jj = 0; jj < 8; ++jj)
+                        if (jj < nc)
+                            o[(size_t)(obase + c0 + jj) * pr.ld_out + m] =
+                                (uint16_t)(pack_bf16x2(__uint_as_float(g[jj]), 0.f) & 0xFFFFu);
                 } else {
                     float *o = static_cast<float *>(pr.out);
 #pragma unroll
-                    for (int j = 0; j < 8; ++j)
-                        if (j < nc) o[(size_t)(obase + c0 + j) * pr.ld_out + m] = __uint_as_float(g[j]);
+                    for (int jj = 0; jj < 8; ++jj)
+                        if (jj < nc) {
+                            o[(size_t)(obase + c0 + jj) * pr.ld_out + m] = __uint_as_float(g[jj]);
+                            if (pr.n_mat == 2)
+                                o[(size_t)(obase + c0 + jj) * pr.ld_out + pr.mat_col + m] = __uint_as_float(u[jj]);
+                        }
                 }
             }
             tc_fence_before();
             __syncwarp();
+            if (tid == 384) trace_put(P, 6, tile);
             if (lane == 0) mbar_arrive(&S->acc_empty[ab]);
         }
     }

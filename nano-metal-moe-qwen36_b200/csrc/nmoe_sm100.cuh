@@ -37,6 +37,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait with a suspend-time hint (ns): the thread sleeps in hardware until the phase
+// completes or the hint expires, instead of spinning on issue slots.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Every wait loop is capped by an iteration count as well as by the deadline, so
 // termination never depends on %globaltimer advancing.
 constexpr uint32_t kMaxSpins = 1u << 22;
@@ -46,6 +60,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint64
         if (it >= kMaxSpins || globaltimer_ns() > deadline) return false;
         if (it > 32) __nanosleep(32);
     }
+    return true;
+}
+// Sleeping wait for the grouped GEMM's role warps: each try suspends up to 20 us.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity, uint64_t deadline) {
+    for (uint32_t it = 0; !mbar_try_wait_sleep(bar, parity, 20000u); ++it)
+        if (it >= (1u << 16) || globaltimer_ns() > deadline) return false;
     return true;
 }
 // Warp-uniform: all 32 lanes must call; all get the same answer.

@@ -29,7 +29,7 @@ ABI_SYMBOLS = (
     "nmoe_moe_load_layer", "nmoe_moe_load_layer_file", "nmoe_moe_set_dense",
     "nmoe_moe_forward", "nmoe_moe_route", "nmoe_moe_forward_batched", "nmoe_moe_device_status",
     "nmoe_moe_forward_static", "nmoe_moe_static_error", "nmoe_moe_debug_trail", "nmoe_moe_debug_timeline",
-    "nmoe_moe_debug_logits",
+    "nmoe_moe_debug_logits", "nmoe_moe_debug_gemm_trace",
 )
 
 
@@ -112,6 +112,8 @@ def lib() -> C.CDLL:
     L.nmoe_moe_debug_timeline.argtypes = [vp, vp, i]
     L.nmoe_moe_debug_logits.restype = i
     L.nmoe_moe_debug_logits.argtypes = [vp, vp, i]
+    L.nmoe_moe_debug_gemm_trace.restype = i
+    L.nmoe_moe_debug_gemm_trace.argtypes = [vp, vp, i]
     _lib = L
     return L
 
@@ -220,6 +222,12 @@ class Context:
         """Router logits [T][256] of the last forward_batched call."""
         out = np.zeros((T, 256), np.float32)
         self._check(self._L.nmoe_moe_debug_logits(self.h, out.ctypes.data, T))
+        return out
+
+    def debug_gemm_trace(self):
+        """[13][1024] %clock stamps of CTA 0 of the traced grouped-GEMM launch."""
+        out = np.zeros((13, 1024), np.uint32)
+        self._check(self._L.nmoe_moe_debug_gemm_trace(self.h, out.ctypes.data, out.size))
         return out
 
     def debug_trail(self, n=1024):
