@@ -10,6 +10,7 @@ plus router and shared expert (21.5 MB), so a step touches ~860 MB, far above th
 126 MB L2 (no flush needed; said in `config`).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  python bench.py --workload batched --tokens T     (T tokens a call)
 
 ours: `value` = layer calls / s with inputs resident in HBM (CUDA graph of the 40
 calls, timed with CUDA events, max over ranks); `e2e` = the same metric through the C
@@ -18,6 +19,10 @@ reference: the CPU restatement of the reference's block (oracle, OpenMP over all
 host cores) on a bounded sample of the same workload.
 N > 1: batch-1 decode does not shard (one token); each rank runs an independent
 replica on its own GPU ("replicas only"), value = all ranks' layer calls / max time.
+
+--workload batched (config 2): T tokens [T, 2048] bf16 through the MoE block of each
+of --layers resident layers per step (nmoe_moe_forward_batched: routing, expert-order
+permutation, tcgen05 grouped GEMMs with in-TMEM dequant, combine); value = tokens/s/layer.
 """
 from __future__ import annotations
 
@@ -214,6 +219,158 @@ def run_reference(args, rank, world):
     }
 
 
+# ------------------------------------------------------------------ batched ----
+
+def batched_flops(T: int, k: int) -> float:
+    """Algorithmic FLOPs of one T-token block: routed gate/up/down for k experts per
+    token, the shared expert, the router."""
+    return 2.0 * T * (k * 3 * INTER * HIDDEN + 3 * INTER * HIDDEN + EXPERTS * HIDDEN)
+
+
+def run_batched(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    import nmoe_b200 as N
+    from oracle import oracle as O
+
+    if world > 1:
+        raise SystemExit("--workload batched runs on one GPU in this build (expert parallelism is not built)")
+    dev = local_rank
+    torch.cuda.set_device(dev)
+    bits, k, rdt, sdt = 4, 8, N.DTYPE_BF16, N.DTYPE_BF16
+    T, L = args.tokens, args.batched_layers
+    layers, _ = build_workload(L, bits, k, rdt, sdt, pool=args.pool, seed=args.seed + rank)
+    ctx = N.Context(quant_bits=bits, num_layers=L, router_dtype=rdt, shared_dtype=sdt, t_max=T, device=dev)
+    for l, lw in enumerate(layers):
+        ctx.load_layer(l, lw.experts)
+        ctx.set_dense(l, lw.router, lw.shared_gate, lw.shared_up, lw.shared_down, lw.shared_gate_vec)
+    cpu_layer = layers[0]
+    for lw in layers[1:]:
+        lw.experts = None
+    rng = np.random.default_rng(args.seed + 7)
+    x_h = O.f32_to_bf16(rng.standard_normal((T, HIDDEN), dtype=np.float32))
+    x = torch.from_numpy(x_h.view(np.int16)).to(f"cuda:{dev}")
+    outs = torch.zeros((L, T, HIDDEN), dtype=torch.float32, device=f"cuda:{dev}")
+    idx = torch.zeros((T, 8), dtype=torch.int32, device=f"cuda:{dev}")
+    stream = torch.cuda.Stream(device=dev)
+
+    def step(s):
+        for l in range(L):
+            ctx.forward_batched(l, T, k, x, outs[l], idx_out=idx if l == 0 else None, stream=s)
+
+    with torch.cuda.stream(stream):
+        step(stream.cuda_stream)
+    stream.synchronize()
+    rc, code = ctx.device_status()
+    if rc != N.OK:
+        raise RuntimeError(f"device error word {code} after the first step")
+    distinct = int(np.unique(idx.cpu().numpy()[:, :k]).size)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step(torch.cuda.current_stream().cuda_stream)
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(dev)
+    clocks.start()
+    time.sleep(0.3)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(args.steps):
+            graph.replay()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    per_call_s = ms / 1e3 / (args.steps * L)
+    value = T / per_call_s
+
+    # e2e: pinned host tokens in, outputs read back, every step, through the C ABI
+    x_pin = torch.from_numpy(x_h.view(np.int16)).pin_memory()
+    out_pin = torch.zeros((L, T, HIDDEN), dtype=torch.float32).pin_memory()
+    e2e_steps = max(1, args.steps // 4)
+
+    def step_e2e():
+        with torch.cuda.stream(stream):
+            x.copy_(x_pin, non_blocking=True)
+            step(stream.cuda_stream)
+            out_pin.copy_(outs, non_blocking=True)
+        stream.synchronize()
+
+    for _ in range(2):
+        step_e2e()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        step_e2e()
+    e2e_el = time.perf_counter() - t0
+    e2e_value = e2e_steps * L * T / e2e_el
+
+    # correctness of the timed outputs: a sample of layer-0 tokens against the oracle on
+    # the GPU's own logits
+    sample = list(range(0, T, max(1, T // 8)))[:8]
+    ctx.forward_batched(0, T, k, x, outs[0])
+    torch.cuda.synchronize()
+    lg = ctx.debug_logits(T)
+    got = outs[0].cpu().numpy()
+    errs = []
+    for t in sample:
+        ref = O.block_forward(cpu_layer, k, O.bf16_to_f32(x_h[t]), logits_override=lg[t])
+        errs.append(float(np.linalg.norm(got[t] - ref["out"]) / np.linalg.norm(ref["out"])))
+    rel = max(errs)
+    if rel > 1e-2:
+        raise RuntimeError(f"timed output disagrees with the oracle: rel_l2={rel}")
+
+    esz = {4: 1769472, 2: 983040}[bits]
+    dense = algorithmic_bytes(bits, 0, rdt, sdt) - HIDDEN * 2 - HIDDEN * 4
+    abytes = distinct * esz + dense + T * HIDDEN * (2 + 4)
+    flops = batched_flops(T, k)
+    hbm, hbm_kind = peaks()
+    try:
+        tf = float(json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json")))["bf16_tflops"])
+        tf_kind = "measured"
+    except Exception:
+        tf, tf_kind = 1590.0, "fallback"
+    gbs = abytes / per_call_s / 1e9
+    tfs = flops / per_call_s / 1e12
+    if gbs / hbm >= tfs / tf:
+        roof = {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                "peak_kind": hbm_kind, "algorithmic_bytes_per_launch": abytes}
+    else:
+        roof = {"bound": "tensor", "achieved": tfs, "peak": tf, "unit": "TFLOP/s", "frac": tfs / tf,
+                "peak_kind": tf_kind, "algorithmic_flops_per_launch": flops}
+    roof["traffic"] = profiled_traffic(f"batched_block_T{T}")
+    roof["other_bound"] = {"hbm_frac": gbs / hbm, "tensor_frac": tfs / tf}
+    cpu = None
+    n_cpu = min(T, 8)
+    t0 = time.perf_counter()
+    O.block_forward_batched(cpu_layer, k, O.bf16_to_f32(x_h[:n_cpu]))
+    cel = time.perf_counter() - t0
+    cpu = {"value": n_cpu / cel, "unit": "tokens/s/layer", "cores": O.lib().orc_get_threads(), "kind": "port",
+           "sample": f"{n_cpu} tokens of the same block (oracle, OpenMP over tokens) in {cel:.2f}s"}
+    result = {
+        "metric": "routed-MoE tokens/s/layer (batched)", "value": value, "unit": "tokens/s/layer", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16 operands (q4 dequantised in TMEM), f32 accumulate",
+        "data": "synthetic (seeded bf16 ~N(0,0.02) weights quantised by the reference quantiser rule; "
+                f"{args.pool} distinct expert packs placed in 256 slots per layer; x ~N(0,1) bf16)",
+        "config": {"workload": f"config2 batched MoE block, T={T}, q4 experts, k=8, bf16 router/shared",
+                   "tokens": T, "layers": L, "distinct_experts_routed": distinct,
+                   "l2": "weights of a step exceed L2 (each layer's experts are separate HBM copies)",
+                   "timing": "CUDA graph of one step (all layers), CUDA events"},
+        "roofline": roof,
+        "cpu_baseline": cpu,
+        "e2e": {"value": e2e_value, "unit": "tokens/s/layer", "h2d_bytes_per_step": T * HIDDEN * 2,
+                "d2h_bytes_per_step": L * T * HIDDEN * 4},
+        "gpu_launches": args.steps * L * 9,
+        "clocks": clk,
+        "check": {"rel_l2_max_sample": rel, "tokens_checked": len(sample)},
+    }
+    ctx.close()
+    return result
+
+
 # ---------------------------------------------------------------------- ours ----
 
 def run_ours(args, rank, world, local_rank):
@@ -370,6 +527,9 @@ def main():
     ap.add_argument("--pool", type=int, default=32, help="distinct expert packs generated on the host")
     ap.add_argument("--seed", type=int, default=2026)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--workload", choices=["decode", "batched"], default="decode")
+    ap.add_argument("--tokens", type=int, default=4096, help="T for --workload batched")
+    ap.add_argument("--batched-layers", type=int, default=4, help="resident layers cycled by --workload batched")
     ap.add_argument("--prefetch", action="store_true",
                     help="let each layer call prefetch the next layer's router/shared weights to L2")
     args = ap.parse_args()
@@ -387,7 +547,7 @@ def main():
         import torch.distributed as dist
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local_rank}"))
-    res = run_ours(args, rank, world, local_rank)
+    res = (run_batched if args.workload == "batched" else run_ours)(args, rank, world, local_rank)
     if res is not None:
         print(json.dumps(res), flush=True)
     if world > 1:

@@ -22,9 +22,9 @@
 //
 // Warp roles (512 threads, one CTA per SM, persistent over the item list):
 //   warp 0      TMA producer: raw weight tiles + scale/bias tiles
-//   warp 1      MMA issuer (one thread) and TMEM owner
+//   warp 1      MMA issuer for matrix 0 (one thread) and TMEM owner
 //   warp 2      B loader: TMA tiles of token rows (16 rows x 64 columns)
-//   warp 3      idle
+//   warp 3      MMA issuer for matrix 1 (one thread)
 //   warps 4-11  dequant: raw tile -> bf16 A rows in TMEM
 //   warps 12-15 epilogue: TMEM -> registers -> SwiGLU / store
 // Every mbarrier wait is bounded; on timeout the CTA records kErrTimeout, drains what it
@@ -45,7 +45,7 @@ constexpr int kGemmThreads = 512;
 constexpr int kGemmNChunk = 128;       // tokens per item (MMA N <= 128)
 constexpr int kGemmMaxGroups = 256;
 constexpr int kGemmMaxProblems = 2;
-constexpr int kGemmSA = 4, kGemmSB = 4, kGemmSS = 2;   // kGemmSS scale stages per dequant group
+constexpr int kGemmSA = 4, kGemmSB = 6, kGemmSS = 2;   // kGemmSS scale stages per dequant group
 constexpr int kGemmMaxSlots = 16;
 constexpr uint32_t kGemmAccCols = 256; // accumulators: TMEM columns [0, 256)
 constexpr uint32_t kGemmACols = 64;    // one A stage: 2 matrices x 32 columns (bf16 pairs)
@@ -426,7 +426,7 @@ struct GemmSmem {
     uint64_t a_full[kGemmSA], a_empty[kGemmSA];
     uint64_t b_full[kGemmSB], b_empty[kGemmSB];
     uint64_t acc_full[2], acc_empty[2];
-    uint64_t drain;
+    uint64_t drain[2];
     uint32_t tmem_base;
     int abort;
     GemmTables T;
@@ -468,6 +468,117 @@ __host__ __device__ __forceinline__ int kperm_pos(int col) {
     return (col & ~7) | (j < 4 ? 2 * j : 2 * (j - 4) + 1);
 }
 
+// State of one dequant thread across items: ring positions and its place in the CTA.
+struct DqCtx {
+    GemmSmem *S;
+    uint8_t *sRaw, *sSc;
+    int SR, grp, r;
+    uint32_t tlane;          // TMEM lane of row r, first A-stage column
+    uint64_t deadline;
+    uint32_t *trace_a;       // trace rows for one thread, or nullptr
+    Ring raw{kGemmMaxSlots}, sc{kGemmSS}, a{kGemmSA};
+    uint32_t gstep = 0;      // steps seen so far (both groups): parity picks the group
+};
+
+__device__ __forceinline__ void dq_trace(const DqCtx &D, int row, uint32_t i) {
+    if (D.trace_a != nullptr && blockIdx.x == 0 && i < (uint32_t)kTraceRow) {
+        uint32_t c;
+        asm volatile("mov.u32 %0, %%clock;" : "=r"(c));
+        D.trace_a[row * kTraceRow + i] = c;
+    }
+}
+
+// One pass over the steps [ks0, ks0 + kb) of an item, q4/q2 weights.
+template <int kFmt, int kNMat, bool kSplit>
+__device__ bool dq_run_q(DqCtx &D, const StepGeo &G, int ks0, bool lo) {
+    GemmSmem *S = D.S;
+    const int lane = threadIdx.x & 31;
+    int lastw = -1;
+    for (int j = 0; j < G.kb; ++j, ++D.gstep) {
+        if ((int)(D.gstep & 1) != D.grp) {   // the other group's step: advance the rings
+            D.raw.next();
+            D.a.next();
+            continue;
+        }
+        const int ks = ks0 + j;
+        dq_trace(D, 10, D.a.count);
+        if (!__all_sync(0xffffffffu, mbar_wait_sleep(&S->a_empty[D.a.idx], D.a.phase ^ 1, D.deadline))) return false;
+        tc_fence_after();
+        dq_trace(D, 11, D.a.count);
+        const int si = D.grp * kGemmSS + D.sc.idx;
+        if ((ks >> 3) != lastw) {
+            lastw = ks >> 3;
+            if (!__all_sync(0xffffffffu, mbar_wait_sleep(&S->sc_full[si], D.sc.phase, D.deadline))) return false;
+        }
+        if (!__all_sync(0xffffffffu, mbar_wait_sleep(&S->raw_full[D.raw.idx], D.raw.phase, D.deadline))) return false;
+        if (S->abort) return false;
+        dq_trace(D, 2, D.a.count);
+        const uint8_t *src = D.sRaw + D.raw.idx * kGemmSlot + D.r * G.rowb;
+        const uint8_t *scp = D.sSc + si * 2 * kGemmScStage;
+        const int sidx = D.r * 8 + (ks & 7);
+        const uint32_t ta = D.tlane + D.a.idx * kGemmACols;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            if (kSplit) dq_step_split<kFmt>(src, scp, sidx, ta + 16 * hh, hh, lo);
+            else dq_step_q<kFmt, kNMat>(src, G.rawm, scp, sidx, ta + 16 * hh, hh);
+        }
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        // last step of this group in the scale window: the group's next step is 2 on
+        const bool rel_sc = ((ks + 2) >> 3) != (ks >> 3) || j + 2 >= G.kb;
+        dq_trace(D, 3, D.a.count);
+        if (lane == 0) {
+            mbar_arrive(&S->a_full[D.a.idx]);
+            mbar_arrive(&S->raw_empty[D.raw.idx]);
+            if (rel_sc) mbar_arrive(&S->sc_empty[si]);
+        }
+        if (rel_sc) {
+            D.sc.next();
+            lastw = -1;
+        }
+        D.raw.next();
+        D.a.next();
+    }
+    return true;
+}
+
+// One pass over an item's steps, bf16 weights (nslot raw slots a step; this thread's
+// rows sit in slot r / rows-per-slot).
+template <int kNMat>
+__device__ bool dq_run_bf16(DqCtx &D, const StepGeo &G, int ks0, bool zero) {
+    GemmSmem *S = D.S;
+    const int lane = threadIdx.x & 31;
+    const int rps = 128 / G.nslot, qs = D.r / rps;
+    for (int j = 0; j < G.kb; ++j, ++D.gstep) {
+        if ((int)(D.gstep & 1) != D.grp) {
+            for (int k = 0; k < G.nslot; ++k) D.raw.next();
+            D.a.next();
+            continue;
+        }
+        if (!__all_sync(0xffffffffu, mbar_wait_sleep(&S->a_empty[D.a.idx], D.a.phase ^ 1, D.deadline))) return false;
+        tc_fence_after();
+        const uint32_t slot = D.raw.idx + qs < (uint32_t)D.SR ? D.raw.idx + qs : D.raw.idx + qs - D.SR;
+        const uint32_t ph = D.raw.idx + qs < (uint32_t)D.SR ? D.raw.phase : D.raw.phase ^ 1;
+        if (!__all_sync(0xffffffffu, mbar_wait_sleep(&S->raw_full[slot], ph, D.deadline))) return false;
+        if (S->abort) return false;
+        const uint8_t *src = D.sRaw + slot * kGemmSlot + (D.r - qs * rps) * 128;
+        const uint32_t ta = D.tlane + D.a.idx * kGemmACols;
+        dq_step_bf16<kNMat>(src, G.rawm, ta, zero);
+        dq_step_bf16<kNMat>(src + 64, G.rawm, ta + 16, zero);
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+            mbar_arrive_n(&S->raw_empty[slot], 4 * 32 / rps);   // four arrivals complete a slot
+            mbar_arrive(&S->a_full[D.a.idx]);
+        }
+        for (int k = 0; k < G.nslot; ++k) D.raw.next();
+        D.a.next();
+    }
+    return true;
+}
+
 __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_constant__ GemmParams P) {
     extern __shared__ __align__(1024) uint8_t smraw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
@@ -483,10 +594,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
     if (tid == 0) {
         for (int i = 0; i < SR; ++i) { mbar_init(&S->raw_full[i], 1); mbar_init(&S->raw_empty[i], 4); }
         for (int i = 0; i < 2 * kGemmSS; ++i) { mbar_init(&S->sc_full[i], 1); mbar_init(&S->sc_empty[i], 4); }
-        for (int i = 0; i < kGemmSA; ++i) { mbar_init(&S->a_full[i], 4); mbar_init(&S->a_empty[i], 1); }
-        for (int i = 0; i < kGemmSB; ++i) { mbar_init(&S->b_full[i], 1); mbar_init(&S->b_empty[i], 1); }
-        for (int i = 0; i < 2; ++i) { mbar_init(&S->acc_full[i], 1); mbar_init(&S->acc_empty[i], 4); }
-        mbar_init(&S->drain, 1);
+        // a_empty / b_empty / acc_full: one commit from each of the two MMA issuers
+        for (int i = 0; i < kGemmSA; ++i) { mbar_init(&S->a_full[i], 4); mbar_init(&S->a_empty[i], 2); }
+        for (int i = 0; i < kGemmSB; ++i) { mbar_init(&S->b_full[i], 1); mbar_init(&S->b_empty[i], 2); }
+        for (int i = 0; i < 2; ++i) { mbar_init(&S->acc_full[i], 2); mbar_init(&S->acc_empty[i], 4); }
+        mbar_init(&S->drain[0], 1);
+        mbar_init(&S->drain[1], 1);
         S->abort = 0;
         mbar_fence_init();
     }
@@ -564,9 +677,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
             raw.drain(S->raw_full, deadline);
             sc0.drain(S->sc_full, deadline);
             sc1.drain(S->sc_full + kGemmSS, deadline);
+        } else if (lane == 1 && P.trace != nullptr && blockIdx.x == 0) {
+            // diagnostics only: record when each raw slot's data lands
+            Ring raw(SR);
+            for (int it = blockIdx.x; it < n_items && !S->abort; it += gridDim.x) {
+                const GemmItem w = gemm_item(P, &S->T, it);
+                const GemmProblem &pr = P.prob[w.p];
+                const StepGeo G = step_geo(pr.fmt, pr.n_mat, pr.K, pr.ksplit);
+                const int slots = __popc(pr.passes) * G.kb * G.nslot;
+                for (int q = 0; q < slots; ++q) {
+                    if (!mbar_wait_sleep(&S->raw_full[raw.idx], raw.phase, deadline)) break;
+                    trace_put(P, 7, raw.count);
+                    raw.next();
+                }
+            }
         }
-    } else if (warp == 1) {
-        // ------------------------------------------------ MMA issuer ----
+    } else if (warp == 1 || warp == 3) {
+        // ------------------------------------------------ MMA issuers ----
+        // A thread issues ~one tcgen05.mma every 46 cycles, so two threads share the work:
+        // warp 1 issues matrix 0 (gate), warp 3 matrix 1 (up). Both commit every stage
+        // release; for single-matrix problems warp 3 only adds its arrivals.
+        const int mat = warp == 1 ? 0 : 1;
         if (lane == 0) {
             Ring a(kGemmSA), b(kGemmSB);
             uint32_t tile = 0;
@@ -576,25 +707,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
                 const GemmProblem &pr = P.prob[w.p];
                 const StepGeo G = step_geo(pr.fmt, pr.n_mat, pr.K, pr.ksplit);
                 const int steps = __popc(pr.passes) * G.kb;
+                const bool mine = mat < pr.n_mat;
                 const int ab = tile % P.acc_bufs;
                 if (!mbar_wait_sleep(&S->acc_empty[ab], ((tile / P.acc_bufs) & 1) ^ 1, deadline)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t idesc = idesc_bf16((w.n + 15) & ~15);
-                const uint32_t d0 = tmem + ab * 128;   // accumulator, matrix 0
+                const uint32_t d = tmem + ab * 128 + mat * 128;   // this issuer's accumulator
                 for (int s = 0; s < steps; ++s) {
                     if (!mbar_wait_sleep(&S->b_full[b.idx], b.phase, deadline)) { ok = false; break; }
-                    trace_put(P, 8, a.count);
+                    if (mat == 0) trace_put(P, 8, a.count);
                     if (!mbar_wait_sleep(&S->a_full[a.idx], a.phase, deadline)) { ok = false; break; }
                     tc_fence_after();
-                    trace_put(P, 4, a.count);
-                    const uint64_t bd = sw128_desc(smem_u32(sB + b.idx * kGemmBStage));
-                    const uint32_t a0 = tmem + kGemmAccCols + a.idx * kGemmACols;   // A stage, matrix 0
+                    if (mat == 0) trace_put(P, 4, a.count);
+                    if (mine) {
+                        const uint64_t bd = sw128_desc(smem_u32(sB + b.idx * kGemmBStage));
+                        const uint32_t a0 = tmem + kGemmAccCols + a.idx * kGemmACols + mat * 32;
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) {
-                        tc_mma_ts(d0, a0 + 8 * kk, bd + 2 * kk, idesc, (s | kk) ? 1u : 0u);
-                        if (pr.n_mat == 2) tc_mma_ts(d0 + 128, a0 + 32 + 8 * kk, bd + 2 * kk, idesc, (s | kk) ? 1u : 0u);
+                        for (int kk = 0; kk < 4; ++kk) tc_mma_ts(d, a0 + 8 * kk, bd + 2 * kk, idesc, (s | kk) ? 1u : 0u);
+                        issued = true;
                     }
-                    issued = true;
                     tc_commit(&S->a_empty[a.idx]);
                     tc_commit(&S->b_empty[b.idx]);
                     a.next();
@@ -604,9 +735,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
                 tc_commit(&S->acc_full[ab]);
             }
             if (!ok) gemm_fail(S, P.err);
-            if (issued) {   // every MMA issued has completed before TMEM is freed
-                tc_commit(&S->drain);
-                mbar_wait_sleep(&S->drain, 0, deadline + 100000000ull);
+            if (issued) {   // every MMA this thread issued has completed before TMEM is freed
+                tc_commit(&S->drain[mat]);
+                mbar_wait_sleep(&S->drain[mat], 0, deadline + 100000000ull);
             }
         }
     } else if (warp == 2) {
@@ -636,117 +767,40 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
             if (!ok) gemm_fail(S, P.err);
             b.drain(S->b_full, deadline);
         }
-    } else if (warp == 3) {
-        // diagnostics only: with tracing on, record when each raw slot's data lands
-        if (P.trace != nullptr && blockIdx.x == 0 && lane == 0) {
-            Ring raw(SR);
-            for (int it = blockIdx.x; it < n_items && !S->abort; it += gridDim.x) {
-                const GemmItem w = gemm_item(P, &S->T, it);
-                const GemmProblem &pr = P.prob[w.p];
-                const StepGeo G = step_geo(pr.fmt, pr.n_mat, pr.K, pr.ksplit);
-                const int steps = __popc(pr.passes) * G.kb;
-                const int slots = pr.fmt != kAFmtBf16 ? steps / G.sps : steps * G.nslot;
-                for (int q = 0; q < slots; ++q) {
-                    if (!mbar_wait_sleep(&S->raw_full[raw.idx], raw.phase, deadline)) break;
-                    trace_put(P, 7, raw.count);
-                    raw.next();
-                }
-            }
-        }
     } else if (warp < 12) {
         // ------------------------------------------------ dequant (2 x 128 threads) ----
         // Two groups of four warps take alternate steps, so one group's barrier waits
         // overlap the other's conversion. A thread converts one full row of a step.
         const int grp = (warp - 4) >> 2, r = 32 * (warp & 3) + lane;
-        const uint32_t tlane = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + kGemmAccCols;
-        Ring raw(SR), sc(kGemmSS), a(kGemmSA);
-        uint32_t gstep = 0;
+        DqCtx D;
+        D.S = S;
+        D.sRaw = sRaw;
+        D.sSc = sSc;
+        D.SR = SR;
+        D.grp = grp;
+        D.r = r;
+        D.tlane = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + kGemmAccCols;
+        D.deadline = deadline;
+        D.trace_a = (warp == 4 && lane == 0) ? P.trace : nullptr;
+        D.raw.n = (uint32_t)SR;
         bool ok = true;
         for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
             const GemmItem w = gemm_item(P, &S->T, it);
             const GemmProblem &pr = P.prob[w.p];
             const StepGeo G = step_geo(pr.fmt, pr.n_mat, pr.K, pr.ksplit);
-            const bool q = pr.fmt != kAFmtBf16;
             const int npass = __popc(pr.passes), ks0 = w.sp * G.kb;
-            const int rps = 128 / G.nslot, qs = r / rps;   // bf16: slot holding this row
             for (int ps = 0; ps < npass && ok; ++ps) {
                 const bool lo = gemm_pass(pr.passes, ps) == 2;
-                int lastw = -1;
-                for (int j = 0; j < G.kb; ++j, ++gstep) {
-                    const int ks = ks0 + j;
-                    if ((int)(gstep & 1) != grp) {   // the other group's step: advance the rings
-                        for (int k = 0; k < G.nslot; ++k) raw.next();
-                        a.next();
-                        continue;
-                    }
-                    if (lane == 0 && warp == 4) trace_put(P, 10, a.count);
-                    if (!__all_sync(0xffffffffu, mbar_wait_sleep(&S->a_empty[a.idx], a.phase ^ 1, deadline))) { ok = false; break; }
-                    tc_fence_after();
-                    if (lane == 0 && warp == 4) trace_put(P, 11, a.count);
-                    const uint32_t ta = tlane + a.idx * kGemmACols;
-                    if (!q) {
-                        const uint32_t slot = raw.idx + qs < (uint32_t)SR ? raw.idx + qs : raw.idx + qs - SR;
-                        const uint32_t ph = raw.idx + qs < (uint32_t)SR ? raw.phase : raw.phase ^ 1;
-                        if (!__all_sync(0xffffffffu, mbar_wait_sleep(&S->raw_full[slot], ph, deadline))) { ok = false; break; }
-                        const uint8_t *src = sRaw + slot * kGemmSlot + (r - qs * rps) * 128;
-                        if (pr.n_mat == 2) {
-                            dq_step_bf16<2>(src, G.rawm, ta, pr.split && lo);
-                            dq_step_bf16<2>(src + 64, G.rawm, ta + 16, pr.split && lo);
-                        } else {
-                            dq_step_bf16<1>(src, G.rawm, ta, pr.split && lo);
-                            dq_step_bf16<1>(src + 64, G.rawm, ta + 16, pr.split && lo);
-                        }
-                        tc_wait_st();
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) {
-                            mbar_arrive_n(&S->raw_empty[slot], 4 * 32 / rps);   // 4 arrivals per slot
-                            mbar_arrive(&S->a_full[a.idx]);
-                        }
-                        for (int k = 0; k < G.nslot; ++k) raw.next();
-                        a.next();
-                        continue;
-                    }
-                    const int si = grp * kGemmSS + sc.idx;
-                    const bool new_window = (ks >> 3) != lastw;
-                    if (new_window) {
-                        lastw = ks >> 3;
-                        if (!__all_sync(0xffffffffu, mbar_wait_sleep(&S->sc_full[si], sc.phase, deadline))) { ok = false; break; }
-                    }
-                    if (!__all_sync(0xffffffffu, mbar_wait_sleep(&S->raw_full[raw.idx], raw.phase, deadline))) { ok = false; break; }
-                    if (lane == 0 && warp == 4) trace_put(P, 2, a.count);
-                    {
-                        const uint8_t *src = sRaw + raw.idx * kGemmSlot + r * G.rowb;
-                        const uint8_t *scp = sSc + si * 2 * kGemmScStage;
-                        const int sidx = r * 8 + (ks & 7);
-#pragma unroll
-                        for (int hh = 0; hh < 2; ++hh) {
-                            if (pr.fmt == kAFmtQ4) {
-                                if (pr.split) dq_step_split<kAFmtQ4>(src, scp, sidx, ta + 16 * hh, hh, lo);
-                                else if (pr.n_mat == 2) dq_step_q<kAFmtQ4, 2>(src, G.rawm, scp, sidx, ta + 16 * hh, hh);
-                                else dq_step_q<kAFmtQ4, 1>(src, G.rawm, scp, sidx, ta + 16 * hh, hh);
-                            } else {
-                                if (pr.split) dq_step_split<kAFmtQ2>(src, scp, sidx, ta + 16 * hh, hh, lo);
-                                else if (pr.n_mat == 2) dq_step_q<kAFmtQ2, 2>(src, G.rawm, scp, sidx, ta + 16 * hh, hh);
-                                else dq_step_q<kAFmtQ2, 1>(src, G.rawm, scp, sidx, ta + 16 * hh, hh);
-                            }
-                        }
-                    }
-                    tc_wait_st();
-                    tc_fence_before();
-                    __syncwarp();
-                    // last step of this group in the scale window: the next one is 2 steps on
-                    const bool rel_sc = ((ks + 2) >> 3) != (ks >> 3) || j + 2 >= G.kb;
-                    if (lane == 0 && warp == 4) trace_put(P, 3, a.count);
-                    if (lane == 0 && warp == 11) trace_put(P, 9, a.count);
-                    if (lane == 0) {
-                        mbar_arrive(&S->a_full[a.idx]);
-                        mbar_arrive(&S->raw_empty[raw.idx]);
-                        if (rel_sc) mbar_arrive(&S->sc_empty[si]);
-                    }
-                    if (rel_sc) { sc.next(); lastw = -1; }
-                    raw.next();
-                    a.next();
+                if (pr.fmt == kAFmtBf16) {
+                    ok = pr.n_mat == 2 ? dq_run_bf16<2>(D, G, ks0, pr.split && lo) : dq_run_bf16<1>(D, G, ks0, pr.split && lo);
+                } else if (pr.fmt == kAFmtQ4) {
+                    ok = pr.split ? dq_run_q<kAFmtQ4, 1, true>(D, G, ks0, lo)
+                                  : pr.n_mat == 2 ? dq_run_q<kAFmtQ4, 2, false>(D, G, ks0, lo)
+                                                  : dq_run_q<kAFmtQ4, 1, false>(D, G, ks0, lo);
+                } else {
+                    ok = pr.split ? dq_run_q<kAFmtQ2, 1, true>(D, G, ks0, lo)
+                                  : pr.n_mat == 2 ? dq_run_q<kAFmtQ2, 2, false>(D, G, ks0, lo)
+                                                  : dq_run_q<kAFmtQ2, 1, false>(D, G, ks0, lo);
                 }
             }
         }
