@@ -175,6 +175,11 @@ int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int k, const v
                              const float *h_mid, void *out, int out_dtype, uint32_t *idx_out,
                              float *w_out, void *stream);
 
+/* Expert parallelism: fill `out` (>= 128 bytes) with a fresh NCCL unique id. One rank
+ * calls it and hands the bytes to every rank's nmoe_moe_config.nccl_unique_id. No
+ * reference counterpart (the reference runs on one device). */
+int nmoe_moe_nccl_unique_id(void *out, size_t bytes);
+
 /* Read and clear the device error word (synchronises the context's device). Returns
  * NMOE_OK or NMOE_EDEVICE and the first recorded code in *code (may be NULL). */
 int nmoe_moe_device_status(nmoe_moe_ctx *ctx, int *code);

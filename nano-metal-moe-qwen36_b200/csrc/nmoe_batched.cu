@@ -23,6 +23,9 @@
 #include <string.h>
 
 #include <algorithm>
+#include <vector>
+
+#include <nccl.h>
 
 #include "nmoe_batched.cuh"
 #include "nmoe_gemm.cuh"
@@ -56,6 +59,19 @@ struct BatchedState {
     int trace_launch = -1;                   // NMOE_GEMM_TRACE=<0 router | 1 gate/up | 2 down>
     uint32_t *trace = nullptr;               // [kTraceRows][1024]
     int launch_no = 0;
+};
+
+// Expert parallelism (world_size > 1): this rank holds experts [expert_lo, expert_lo +
+// n_local) and exchanges token rows with the other ranks by NCCL send/recv.
+struct EpState {
+    ncclComm_t comm = nullptr;
+    int world = 1, rank = 0;
+    size_t r_cap = 0;            // rows this rank can receive: world * t_max * k_max
+    uint16_t *xr = nullptr;      // [r_cap][2048] received token rows, (source rank, local expert) order
+    uint16_t *yr = nullptr;      // [r_cap][2048] their down outputs
+    int *rcnt = nullptr;         // [world][n_local] rows received per (source, local expert)
+    int *h_cnt = nullptr;        // pinned [256] this rank's counts per global expert
+    int *h_rcnt = nullptr;       // pinned [world * n_local]
 };
 
 }  // namespace nmoe
@@ -447,6 +463,34 @@ int nmoe_batched_init(nmoe_moe_ctx *ctx) {
     const size_t T = (size_t)tm;
     B->rows_cap = std::max(4 * tm, 1024);
     const size_t R = (size_t)B->rows_cap;
+    const int W = ctx->cfg.world_size;
+    size_t act_rows = T * 9;
+    if (W > 1) {
+        EpState *E = new (std::nothrow) EpState();
+        if (E == nullptr) return NMOE_ENOMEM;
+        ctx->ep = E;
+        E->world = W;
+        E->rank = ctx->cfg.rank;
+        E->r_cap = (size_t)W * T * ctx->cfg.k_max;
+        ncclUniqueId id;
+        memcpy(&id, ctx->cfg.nccl_unique_id, sizeof id);
+        const ncclResult_t nr = ncclCommInitRank(&E->comm, W, id, E->rank);
+        if (nr != ncclSuccess) {
+            E->comm = nullptr;
+            nmoe_ctx_set_error(ctx, "ncclCommInitRank: %s", ncclGetErrorString(nr));
+            return NMOE_ENCCL;
+        }
+        act_rows = E->r_cap + T;
+        e = cudaMalloc(&E->xr, E->r_cap * kHidden * 2);
+        if (e == cudaSuccess) e = cudaMalloc(&E->yr, E->r_cap * kHidden * 2);
+        if (e == cudaSuccess) e = cudaMalloc(&E->rcnt, (size_t)kExperts * 4);
+        if (e == cudaSuccess) e = cudaMallocHost(&E->h_cnt, (size_t)kExperts * 4);
+        if (e == cudaSuccess) e = cudaMallocHost(&E->h_rcnt, (size_t)kExperts * 4);
+        if (e != cudaSuccess) {
+            nmoe_ctx_set_error(ctx, "expert-parallel buffers: %s", cudaGetErrorString(e));
+            return e == cudaErrorMemoryAllocation ? NMOE_ENOMEM : NMOE_ECUDA;
+        }
+    }
     struct { void **p; size_t bytes; } al[] = {
         {(void **)&B->xh, T * kHidden * 2},       {(void **)&B->xl, T * kHidden * 2},
         {(void **)&B->xp, T * kMaxK * kHidden * 2},
@@ -454,7 +498,7 @@ int nmoe_batched_init(nmoe_moe_ctx *ctx) {
         {(void **)&B->w, T * kMaxK * 4},          {(void **)&B->idx, T * kMaxK * 4},
         {(void **)&B->rank, T * kMaxK * 4},       {(void **)&B->inv, T * kMaxK * 4},
         {(void **)&B->perm, T * kMaxK * 4},       {(void **)&B->cnt, kExperts * 4},
-        {(void **)&B->act, T * 9 * kInter * 2},   {(void **)&B->y, T * 8 * kHidden * 2},
+        {(void **)&B->act, act_rows * kInter * 2}, {(void **)&B->y, T * 8 * kHidden * 2},
         {(void **)&B->p_router, R * kExperts * 4}, {(void **)&B->p_sgu, R * 2 * kInter * 4},
         {(void **)&B->p_sdown, R * kHidden * 4},
     };
@@ -479,6 +523,16 @@ void nmoe_batched_destroy(nmoe_moe_ctx *ctx) {
         if (p) cudaFree(p);
     delete B;
     ctx->batched = nullptr;
+    if (EpState *E = ctx->ep) {
+        if (E->comm) ncclCommDestroy(E->comm);
+        if (E->xr) cudaFree(E->xr);
+        if (E->yr) cudaFree(E->yr);
+        if (E->rcnt) cudaFree(E->rcnt);
+        if (E->h_cnt) cudaFreeHost(E->h_cnt);
+        if (E->h_rcnt) cudaFreeHost(E->h_rcnt);
+        delete E;
+        ctx->ep = nullptr;
+    }
 }
 
 extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int k, const void *x, int x_dtype,
@@ -504,13 +558,14 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
         nmoe_ctx_set_error(ctx, "x, out and h_mid must be 16-byte aligned");
         return NMOE_EINVAL;
     }
-    if (ctx->cfg.world_size > 1) {
-        nmoe_ctx_set_error(ctx, "expert-parallel forward_batched is not available in this build");
+    EpState *E = ctx->ep;
+    if (ctx->cfg.world_size > 1 && E == nullptr) {
+        nmoe_ctx_set_error(ctx, "expert parallelism needs t_max > 0 at create");
         return NMOE_EINVAL;
     }
     B->last_T = T;
     B->launch_no = 0;
-    if (T == 0) return NMOE_OK;
+    if (T == 0 && E == nullptr) return NMOE_OK;   // with EP, the rank still serves its experts
     Guard guard(ctx->device);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const bool xf32 = x_dtype == NMOE_DTYPE_F32;
@@ -524,7 +579,8 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
     cudaError_t e;
 
     // 1. x planes, counts cleared
-    k_prep<<<(T * 256 + 255) / 256, 256, 0, st>>>(x, xf32, T, B->xh, B->xl, B->cnt);
+    if (T > 0) k_prep<<<(T * 256 + 255) / 256, 256, 0, st>>>(x, xf32, T, B->xh, B->xl, B->cnt);
+    else cudaMemsetAsync(B->cnt, 0, kExperts * sizeof(int), st);
 
     // K slices of the dense problems (router, shared gate/up, shared down)
     const int target = ctx->num_sms;
@@ -533,7 +589,7 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
     const int nsplit_d = pick_ksplit(sfmt, 1, kInter, 16, T, B->rows_cap, target);
 
     // 2. router logits (K-slice partials)
-    {
+    if (T > 0) {
         GemmParams P;
         memset(&P, 0, sizeof P);
         P.n_prob = 1;
@@ -579,8 +635,10 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
         a.T = T;
         a.k = k;
         a.num_experts = ctx->cfg.num_experts;
-        a.expert_lo = ctx->expert_lo;
-        a.n_local = ctx->n_local;
+        // with EP every rank routes over all experts; positions then group the rows by
+        // destination rank
+        a.expert_lo = E ? 0 : ctx->expert_lo;
+        a.n_local = E ? kExperts : ctx->n_local;
         a.idx = B->idx;
         a.w = B->w;
         a.score = B->score;
@@ -589,12 +647,68 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
         a.idx_out = idx_out;
         a.w_out = w_out;
         a.err = ctx->d_err;
-        k_route<<<(T + kRouteWarps - 1) / kRouteWarps, kRouteWarps * 32, 0, st>>>(a);
-        k_scatter<<<(T * k + 255) / 256, 256, 0, st>>>(B->idx, B->rank, B->cnt, T, k, ctx->expert_lo, ctx->n_local,
-                                                       B->perm, B->inv);
-        k_gather_rows<<<T * k, 256, 0, st>>>(B->xh, B->perm, T, k, B->xp);
+        if (T > 0) {
+            k_route<<<(T + kRouteWarps - 1) / kRouteWarps, kRouteWarps * 32, 0, st>>>(a);
+            k_scatter<<<(T * k + 255) / 256, 256, 0, st>>>(B->idx, B->rank, B->cnt, T, k, a.expert_lo, a.n_local,
+                                                           B->perm, B->inv);
+            k_gather_rows<<<T * k, 256, 0, st>>>(B->xh, B->perm, T, k, B->xp);
+        }
     }
-    const int shared_base = T * k;
+    int shared_base = T * k;
+
+    // 3b. expert parallelism: send each rank the rows routed to its experts
+    std::vector<long> soff, scnt, roff, rcnt_s;
+    if (E != nullptr) {
+        const int W = E->world, nl = ctx->n_local;
+        ncclResult_t nr = ncclGroupStart();
+        for (int p = 0; p < W && nr == ncclSuccess; ++p) {
+            nr = ncclSend(B->cnt + p * nl, nl, ncclInt32, p, E->comm, st);
+            if (nr == ncclSuccess) nr = ncclRecv(E->rcnt + p * nl, nl, ncclInt32, p, E->comm, st);
+        }
+        if (nr == ncclSuccess) nr = ncclGroupEnd();
+        if (nr != ncclSuccess) {
+            nmoe_ctx_set_error(ctx, "count exchange: %s", ncclGetErrorString(nr));
+            return NMOE_ENCCL;
+        }
+        cudaMemcpyAsync(E->h_cnt, B->cnt, kExperts * 4, cudaMemcpyDeviceToHost, st);
+        cudaMemcpyAsync(E->h_rcnt, E->rcnt, (size_t)W * nl * 4, cudaMemcpyDeviceToHost, st);
+        if ((e = cudaStreamSynchronize(st)) != cudaSuccess) {   // NCCL needs the sizes on the host
+            nmoe_ctx_set_error(ctx, "count exchange: %s", cudaGetErrorString(e));
+            return NMOE_ECUDA;
+        }
+        soff.assign(W + 1, 0);
+        roff.assign(W + 1, 0);
+        scnt.assign(W, 0);
+        rcnt_s.assign(W, 0);
+        for (int p = 0; p < W; ++p) {
+            for (int j = 0; j < nl; ++j) {
+                scnt[p] += E->h_cnt[p * nl + j];
+                rcnt_s[p] += E->h_rcnt[p * nl + j];
+            }
+            soff[p + 1] = soff[p] + scnt[p];
+            roff[p + 1] = roff[p] + rcnt_s[p];
+        }
+        if ((size_t)roff[W] > E->r_cap) {
+            nmoe_ctx_set_error(ctx, "received %ld rows, capacity %zu", roff[W], E->r_cap);
+            return NMOE_ESIZE;
+        }
+        nr = ncclGroupStart();
+        for (int p = 0; p < W && nr == ncclSuccess; ++p) {
+            if (scnt[p]) nr = ncclSend(B->xp + soff[p] * kHidden, (size_t)scnt[p] * kHidden * 2, ncclChar, p, E->comm, st);
+            if (nr == ncclSuccess && rcnt_s[p])
+                nr = ncclRecv(E->xr + roff[p] * kHidden, (size_t)rcnt_s[p] * kHidden * 2, ncclChar, p, E->comm, st);
+        }
+        if (nr == ncclSuccess) nr = ncclGroupEnd();
+        if (nr != ncclSuccess) {
+            nmoe_ctx_set_error(ctx, "token dispatch: %s", ncclGetErrorString(nr));
+            return NMOE_ENCCL;
+        }
+        shared_base = (int)roff[W];
+    }
+    const int n_groups = E ? E->world * ctx->n_local : ctx->n_local;
+    const int *gcnt = E ? E->rcnt : B->cnt;
+    const int group_mod = E ? ctx->n_local : 0;
+    const size_t act_rows = E ? E->r_cap + (size_t)B->t_max : (size_t)B->t_max * 9;
 
     // 4. gate/up + SwiGLU: routed positions and the shared expert
     {
@@ -607,9 +721,10 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
         r.K = kHidden;
         r.m_tiles = 4;
         r.ksplit = 1;
-        r.n_groups = ctx->n_local;
-        r.cnt = B->cnt;
-        r.b_hi = B->xp;
+        r.n_groups = n_groups;
+        r.cnt = gcnt;
+        r.group_mod = group_mod;
+        r.b_hi = E ? E->xr : B->xp;
         r.passes = kPassHiHi;
         r.epi = kEpiSwiGLU;
         r.ld_out = kInter;
@@ -631,6 +746,7 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
         s.passes = kPassHiHi;
         s.epi = kEpiF32;
         s.ld_out = 2 * kInter;
+        if (T == 0) P.n_prob = 1;
         s.mat_col = kInter;
         s.split_rows = T;
         s.out = B->p_sgu;
@@ -644,7 +760,7 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
             ok = ok && make_matrix_maps(B, s, 0, sp, sfmt, kHidden, ps, 32, 16 * ps, 1, 512 * ps, 0, 0, ps);
             ok = ok && make_matrix_maps(B, s, 1, sp + DA.srow, sfmt, kHidden, ps, 32, 16 * ps, 1, 512 * ps, 0, 0, ps);
         }
-        ok = ok && make_bmaps(B, r, kMaxK * B->t_max) && make_bmaps(B, s, B->t_max);
+        ok = ok && make_bmaps(B, r, E ? (int)E->r_cap : kMaxK * B->t_max) && make_bmaps(B, s, B->t_max);
         if (!ok) {
             nmoe_ctx_set_error(ctx, "gate/up tensor maps");
             return NMOE_ECUDA;
@@ -656,7 +772,8 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
     }
 
     // shared expert activations from the gate/up partials
-    k_shared_act<<<(T * (kInter / 8) * 4 + 255) / 256, 256, 0, st>>>(B->p_sgu, nsplit_g, T, B->act, shared_base);
+    if (T > 0)
+        k_shared_act<<<(T * (kInter / 8) * 4 + 255) / 256, 256, 0, st>>>(B->p_sgu, nsplit_g, T, B->act, shared_base);
 
     // 5. down: routed positions and the shared expert
     {
@@ -669,13 +786,14 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
         r.K = kInter;
         r.m_tiles = 16;
         r.ksplit = 1;
-        r.n_groups = ctx->n_local;
-        r.cnt = B->cnt;
+        r.n_groups = n_groups;
+        r.cnt = gcnt;
+        r.group_mod = group_mod;
         r.b_hi = B->act;
         r.passes = kPassHiHi;
         r.epi = kEpiBf16;
         r.ld_out = kHidden;
-        r.out = B->y;
+        r.out = E ? E->yr : B->y;
         bool ok = make_matrix_maps(B, r, 0, experts + pg.gu_bytes, bits, kInter, pg.wd * 4, 128, pg.db, ctx->n_local,
                                    pg.esz, pg.tile_band_d, pg.tile_band_d + 256, 16);
         GemmProblem &s = P.prob[1];
@@ -693,9 +811,10 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
         s.ld_out = kHidden;
         s.split_rows = T;
         s.out = B->p_sdown;
+        if (T == 0) P.n_prob = 1;
         const uint64_t rs = DA.sdrow;
         ok = ok && make_matrix_maps(B, s, 0, dense + DA.sdown, sfmt, kInter, rs, 128, 16 * rs, 1, 2048 * rs, 256, 272, rs);
-        ok = ok && make_bmaps(B, r, 9 * B->t_max) && make_bmaps(B, s, 9 * B->t_max);
+        ok = ok && make_bmaps(B, r, (int)act_rows) && make_bmaps(B, s, (int)act_rows);
         if (!ok) {
             nmoe_ctx_set_error(ctx, "down tensor maps");
             return NMOE_ECUDA;
@@ -704,6 +823,22 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
             nmoe_ctx_set_error(ctx, "down gemm launch: %s", cudaGetErrorString(e));
             return NMOE_ECUDA;
         }
+    }
+
+    // 5b. expert parallelism: return the down outputs to the ranks that own the tokens
+    if (E != nullptr) {
+        ncclResult_t nr = ncclGroupStart();
+        for (int p = 0; p < E->world && nr == ncclSuccess; ++p) {
+            if (rcnt_s[p]) nr = ncclSend(E->yr + roff[p] * kHidden, (size_t)rcnt_s[p] * kHidden * 2, ncclChar, p, E->comm, st);
+            if (nr == ncclSuccess && scnt[p])
+                nr = ncclRecv(B->y + soff[p] * kHidden, (size_t)scnt[p] * kHidden * 2, ncclChar, p, E->comm, st);
+        }
+        if (nr == ncclSuccess) nr = ncclGroupEnd();
+        if (nr != ncclSuccess) {
+            nmoe_ctx_set_error(ctx, "combine exchange: %s", ncclGetErrorString(nr));
+            return NMOE_ENCCL;
+        }
+        if (T == 0) return NMOE_OK;
     }
 
     // 6. combine
@@ -738,5 +873,13 @@ extern "C" int nmoe_moe_debug_gemm_trace(nmoe_moe_ctx *ctx, uint32_t *out, int n
     }
     Guard guard(ctx->device);
     if (cudaMemcpy(out, ctx->batched->trace, (size_t)n * 4, cudaMemcpyDeviceToHost) != cudaSuccess) return NMOE_ECUDA;
+    return NMOE_OK;
+}
+
+extern "C" int nmoe_moe_nccl_unique_id(void *out, size_t bytes) {
+    if (out == nullptr || bytes < sizeof(ncclUniqueId)) return NMOE_EINVAL;
+    ncclUniqueId id;
+    if (ncclGetUniqueId(&id) != ncclSuccess) return NMOE_ENCCL;
+    memcpy(out, &id, sizeof id);
     return NMOE_OK;
 }

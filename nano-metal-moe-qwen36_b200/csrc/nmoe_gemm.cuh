@@ -69,6 +69,8 @@ struct alignas(64) GemmProblem {
     int n_groups;             // experts (or 1)
     int cnt_const;            // group size when cnt == nullptr
     const int *cnt;           // [n_groups] tokens per group
+    int group_mod;            // weight group of group g = g % group_mod (0: g); expert
+                              // parallelism orders groups (source rank, local expert)
     int in_base;              // B row of position p = in_base + p
     int out_base;             // output row = out_base + position (+ split * split_rows)
     int split_rows;
@@ -252,7 +254,7 @@ struct GemmTables {
 };
 
 struct GemmItem {
-    int p, g, mt, sp, n, pos0;
+    int p, g, e, mt, sp, n, pos0;   // e: weight group (expert) of group g
 };
 
 __device__ __forceinline__ int gemm_group_count(const GemmProblem &pr, int g) {
@@ -308,6 +310,7 @@ __device__ __forceinline__ GemmItem gemm_item(const GemmParams &P, const GemmTab
     w.g = lo;
     li -= ip[lo];
     const GemmProblem &pr = P.prob[w.p];
+    w.e = pr.group_mod ? w.g % pr.group_mod : w.g;
     const int cnt = gemm_group_count(pr, w.g);
     const int chunks = (cnt + kGemmNChunk - 1) / kGemmNChunk;
     const int per_mt = chunks * pr.ksplit;
@@ -645,8 +648,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
                                 mbar_arrive_expect_tx(&S->sc_full[si], pr.n_mat * kGemmScStage);
                                 for (int m = 0; m < pr.n_mat; ++m) {
                                     uint8_t *d = sSc + (si * 2 + m) * kGemmScStage;
-                                    tma_load_4d(d, &pr.ts[m], ks & ~7, 0, w.mt * 8, w.g, &S->sc_full[si]);
-                                    tma_load_4d(d + 2048, &pr.tb[m], ks & ~7, 0, w.mt * 8, w.g, &S->sc_full[si]);
+                                    tma_load_4d(d, &pr.ts[m], ks & ~7, 0, w.mt * 8, w.e, &S->sc_full[si]);
+                                    tma_load_4d(d + 2048, &pr.tb[m], ks & ~7, 0, w.mt * 8, w.e, &S->sc_full[si]);
                                 }
                                 sc.next();
                             }
@@ -655,7 +658,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
                             mbar_arrive_expect_tx(&S->raw_full[raw.idx], pr.n_mat * G.rawm);
                             for (int m = 0; m < pr.n_mat; ++m)
                                 tma_load_4d(sRaw + raw.idx * kGemmSlot + m * G.rawm, &pr.tw[m], ks * G.wpk, 0, w.mt * 8,
-                                            w.g, &S->raw_full[raw.idx]);
+                                            w.e, &S->raw_full[raw.idx]);
                             raw.next();
                         } else {
                             const int bands = 8 / G.nslot;
@@ -664,7 +667,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
                                 mbar_arrive_expect_tx(&S->raw_full[raw.idx], kGemmSlot);
                                 for (int m = 0; m < pr.n_mat; ++m)
                                     tma_load_4d(sRaw + raw.idx * kGemmSlot + m * G.rawm, &pr.tw[m], ks * 64, 0,
-                                                w.mt * 8 + qs * bands, w.g, &S->raw_full[raw.idx]);
+                                                w.mt * 8 + qs * bands, w.e, &S->raw_full[raw.idx]);
                                 raw.next();
                             }
                             if (!ok) break;

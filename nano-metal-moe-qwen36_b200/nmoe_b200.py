@@ -29,7 +29,7 @@ ABI_SYMBOLS = (
     "nmoe_moe_load_layer", "nmoe_moe_load_layer_file", "nmoe_moe_set_dense",
     "nmoe_moe_forward", "nmoe_moe_route", "nmoe_moe_forward_batched", "nmoe_moe_device_status",
     "nmoe_moe_forward_static", "nmoe_moe_static_error", "nmoe_moe_debug_trail", "nmoe_moe_debug_timeline",
-    "nmoe_moe_debug_logits", "nmoe_moe_debug_gemm_trace",
+    "nmoe_moe_debug_logits", "nmoe_moe_debug_gemm_trace", "nmoe_moe_nccl_unique_id",
 )
 
 
@@ -112,10 +112,21 @@ def lib() -> C.CDLL:
     L.nmoe_moe_debug_timeline.argtypes = [vp, vp, i]
     L.nmoe_moe_debug_logits.restype = i
     L.nmoe_moe_debug_logits.argtypes = [vp, vp, i]
+    L.nmoe_moe_nccl_unique_id.restype = i
+    L.nmoe_moe_nccl_unique_id.argtypes = [vp, sz]
     L.nmoe_moe_debug_gemm_trace.restype = i
     L.nmoe_moe_debug_gemm_trace.argtypes = [vp, vp, i]
     _lib = L
     return L
+
+
+def nccl_unique_id() -> bytes:
+    """A fresh 128-byte NCCL unique id for Context(world_size > 1, nccl_unique_id=...)."""
+    buf = C.create_string_buffer(128)
+    rc = lib().nmoe_moe_nccl_unique_id(buf, 128)
+    if rc != OK:
+        raise NmoeError(rc, "ncclGetUniqueId failed")
+    return buf.raw
 
 
 def expert_size(bits: int) -> int:
