@@ -233,14 +233,19 @@ def run_batched(args, rank, world, local_rank):
     import nmoe_b200 as N
     from oracle import oracle as O
 
-    if world > 1:
-        raise SystemExit("--workload batched runs on one GPU in this build (expert parallelism is not built)")
     dev = local_rank
     torch.cuda.set_device(dev)
     bits, k, rdt, sdt = 4, 8, N.DTYPE_BF16, N.DTYPE_BF16
     T, L = args.tokens, args.batched_layers
-    layers, _ = build_workload(L, bits, k, rdt, sdt, pool=args.pool, seed=args.seed + rank)
-    ctx = N.Context(quant_bits=bits, num_layers=L, router_dtype=rdt, shared_dtype=sdt, t_max=T, device=dev)
+    # one model on every rank: with expert parallelism each rank holds a slice of it
+    layers, _ = build_workload(L, bits, k, rdt, sdt, pool=args.pool, seed=args.seed)
+    uid = None
+    if world > 1:   # experts sharded 256/world per rank, tokens exchanged by NCCL
+        obj = [N.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        uid = obj[0]
+    ctx = N.Context(quant_bits=bits, num_layers=L, router_dtype=rdt, shared_dtype=sdt, t_max=T, device=dev,
+                    world_size=world, rank=rank, nccl_unique_id=uid)
     for l, lw in enumerate(layers):
         ctx.load_layer(l, lw.experts)
         ctx.set_dense(l, lw.router, lw.shared_gate, lw.shared_up, lw.shared_down, lw.shared_gate_vec)
@@ -248,7 +253,8 @@ def run_batched(args, rank, world, local_rank):
     for lw in layers[1:]:
         lw.experts = None
     rng = np.random.default_rng(args.seed + 7)
-    x_h = O.f32_to_bf16(rng.standard_normal((T, HIDDEN), dtype=np.float32))
+    x_h = O.f32_to_bf16(np.random.default_rng(args.seed + 7 + 1000 * rank).standard_normal((T, HIDDEN),
+                                                                                           dtype=np.float32))
     x = torch.from_numpy(x_h.view(np.int16)).to(f"cuda:{dev}")
     outs = torch.zeros((L, T, HIDDEN), dtype=torch.float32, device=f"cuda:{dev}")
     idx = torch.zeros((T, 8), dtype=torch.int32, device=f"cuda:{dev}")
@@ -265,12 +271,19 @@ def run_batched(args, rank, world, local_rank):
     if rc != N.OK:
         raise RuntimeError(f"device error word {code} after the first step")
     distinct = int(np.unique(idx.cpu().numpy()[:, :k]).size)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        step(torch.cuda.current_stream().cuda_stream)
+    if world == 1:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step(torch.cuda.current_stream().cuda_stream)
+        run_step = graph.replay
+    else:   # the count exchange synchronises the host each call: no graph
+        def run_step():
+            step(stream.cuda_stream)
     for _ in range(max(args.warmup, 3)):
-        graph.replay()
+        run_step()
     torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
     clocks = ClockSampler(dev)
     clocks.start()
     time.sleep(0.3)
@@ -279,13 +292,19 @@ def run_batched(args, rank, world, local_rank):
     ev0.record(stream)
     with torch.cuda.stream(stream):
         for _ in range(args.steps):
-            graph.replay()
+            run_step()
     ev1.record(stream)
     torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
     clk = clocks.stop()
     ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        tm = torch.tensor([ms], dtype=torch.float64, device=f"cuda:{dev}")
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+        ms = float(tm.item())
     per_call_s = ms / 1e3 / (args.steps * L)
-    value = T / per_call_s
+    value = world * T / per_call_s
 
     # e2e: pinned host tokens in, outputs read back, every step, through the C ABI
     x_pin = torch.from_numpy(x_h.view(np.int16)).pin_memory()
@@ -305,7 +324,11 @@ def run_batched(args, rank, world, local_rank):
     for _ in range(e2e_steps):
         step_e2e()
     e2e_el = time.perf_counter() - t0
-    e2e_value = e2e_steps * L * T / e2e_el
+    if world > 1:
+        te = torch.tensor([e2e_el], dtype=torch.float64, device=f"cuda:{dev}")
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e_el = float(te.item())
+    e2e_value = world * e2e_steps * L * T / e2e_el
 
     # correctness of the timed outputs: a sample of layer-0 tokens against the oracle on
     # the GPU's own logits
@@ -343,12 +366,13 @@ def run_batched(args, rank, world, local_rank):
     roof["traffic"] = profiled_traffic(f"batched_block_T{T}")
     roof["other_bound"] = {"hbm_frac": gbs / hbm, "tensor_frac": tfs / tf}
     cpu = None
-    n_cpu = min(T, 8)
-    t0 = time.perf_counter()
-    O.block_forward_batched(cpu_layer, k, O.bf16_to_f32(x_h[:n_cpu]))
-    cel = time.perf_counter() - t0
-    cpu = {"value": n_cpu / cel, "unit": "tokens/s/layer", "cores": O.lib().orc_get_threads(), "kind": "port",
-           "sample": f"{n_cpu} tokens of the same block (oracle, OpenMP over tokens) in {cel:.2f}s"}
+    if rank == 0 and world == 1:
+        n_cpu = min(T, 8)
+        t0 = time.perf_counter()
+        O.block_forward_batched(cpu_layer, k, O.bf16_to_f32(x_h[:n_cpu]))
+        cel = time.perf_counter() - t0
+        cpu = {"value": n_cpu / cel, "unit": "tokens/s/layer", "cores": O.lib().orc_get_threads(), "kind": "port",
+               "sample": f"{n_cpu} tokens of the same block (oracle, OpenMP over tokens) in {cel:.2f}s"}
     result = {
         "metric": "routed-MoE tokens/s/layer (batched)", "value": value, "unit": "tokens/s/layer", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
@@ -356,9 +380,12 @@ def run_batched(args, rank, world, local_rank):
         "data": "synthetic (seeded bf16 ~N(0,0.02) weights quantised by the reference quantiser rule; "
                 f"{args.pool} distinct expert packs placed in 256 slots per layer; x ~N(0,1) bf16)",
         "config": {"workload": f"config2 batched MoE block, T={T}, q4 experts, k=8, bf16 router/shared",
-                   "tokens": T, "layers": L, "distinct_experts_routed": distinct,
+                   "tokens": T, "tokens_per_rank": T, "layers": L, "distinct_experts_routed": distinct,
+                   "parallelism": f"expert parallel: {EXPERTS // world} experts per GPU, NCCL all-to-all-v dispatch "
+                                  "and combine" if world > 1 else "single GPU",
                    "l2": "weights of a step exceed L2 (each layer's experts are separate HBM copies)",
-                   "timing": "CUDA graph of one step (all layers), CUDA events"},
+                   "timing": "CUDA graph of one step (all layers), CUDA events" if world == 1 else
+                             "CUDA events around the step loop, max over ranks"},
         "roofline": roof,
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": "tokens/s/layer", "h2d_bytes_per_step": T * HIDDEN * 2,
@@ -368,7 +395,7 @@ def run_batched(args, rank, world, local_rank):
         "check": {"rel_l2_max_sample": rel, "tokens_checked": len(sample)},
     }
     ctx.close()
-    return result
+    return result if rank == 0 else None
 
 
 # ---------------------------------------------------------------------- ours ----
@@ -517,6 +544,9 @@ def run_ours(args, rank, world, local_rank):
     return result
 
 
+_JSON_OUT = sys.stdout
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -534,13 +564,19 @@ def main():
                     help="let each layer call prefetch the next layer's router/shared weights to L2")
     args = ap.parse_args()
 
+    # stdout carries exactly one JSON line: libraries (NCCL's version banner, ...) write
+    # to file descriptor 1, so it is pointed at stderr and the JSON goes to a saved copy
+    global _JSON_OUT
+    _JSON_OUT = os.fdopen(os.dup(1), "w")
+    sys.stdout.flush()
+    os.dup2(2, 1)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         res = run_reference(args, rank, world)
         if res is not None:
-            print(json.dumps(res), flush=True)
+            print(json.dumps(res), file=_JSON_OUT, flush=True)
         return
     if world > 1:
         import torch
@@ -549,7 +585,7 @@ def main():
         dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local_rank}"))
     res = (run_batched if args.workload == "batched" else run_ours)(args, rank, world, local_rank)
     if res is not None:
-        print(json.dumps(res), flush=True)
+        print(json.dumps(res), file=_JSON_OUT, flush=True)
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
