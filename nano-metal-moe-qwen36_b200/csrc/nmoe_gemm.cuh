@@ -45,7 +45,10 @@ constexpr int kGemmThreads = 512;
 constexpr int kGemmNChunk = 128;       // tokens per item (MMA N <= 128)
 constexpr int kGemmMaxGroups = 256;
 constexpr int kGemmMaxProblems = 2;
-constexpr int kGemmSA = 4, kGemmSB = 6, kGemmSS = 2;   // kGemmSS scale stages per dequant group
+constexpr int kGemmSA = 4, kGemmSB = kGemmSA, kGemmSS = 2;   // kGemmSS scale stages per dequant group
+// A step's A stage (TMEM) and B stage (shared memory) share one ring position: one MMA
+// commit frees both, and the dequant warps wait for the B tile before they mark the step
+// ready, so the MMA issuer waits on a single barrier per step.
 constexpr int kGemmMaxSlots = 16;
 constexpr uint32_t kGemmAccCols = 256; // accumulators: TMEM columns [0, 256)
 constexpr uint32_t kGemmACols = 64;    // one A stage: 2 matrices x 32 columns (bf16 pairs)
@@ -427,7 +430,7 @@ struct GemmSmem {
     uint64_t raw_full[kGemmMaxSlots], raw_empty[kGemmMaxSlots];
     uint64_t sc_full[2 * kGemmSS], sc_empty[2 * kGemmSS];   // [group][stage]
     uint64_t a_full[kGemmSA], a_empty[kGemmSA];
-    uint64_t b_full[kGemmSB], b_empty[kGemmSB];
+    uint64_t b_full[kGemmSB];
     uint64_t acc_full[2], acc_empty[2];
     uint64_t drain[2];
     uint32_t tmem_base;
@@ -491,6 +494,14 @@ __device__ __forceinline__ void dq_trace(const DqCtx &D, int row, uint32_t i) {
     }
 }
 
+// The step's B tile has landed (lane 0 waits; the warp agrees).
+__device__ __forceinline__ bool dq_wait_b(const DqCtx &D) {
+    const int lane = threadIdx.x & 31;
+    bool ok = true;
+    if (lane == 0) ok = mbar_wait_sleep(&D.S->b_full[D.a.idx], D.a.phase, D.deadline);
+    return __all_sync(0xffffffffu, ok);
+}
+
 // One pass over the steps [ks0, ks0 + kb) of an item, q4/q2 weights.
 template <int kFmt, int kNMat, bool kSplit>
 __device__ bool dq_run_q(DqCtx &D, const StepGeo &G, int ks0, bool lo) {
@@ -531,6 +542,7 @@ __device__ bool dq_run_q(DqCtx &D, const StepGeo &G, int ks0, bool lo) {
         // last step of this group in the scale window: the group's next step is 2 on
         const bool rel_sc = ((ks + 2) >> 3) != (ks >> 3) || j + 2 >= G.kb;
         dq_trace(D, 3, D.a.count);
+        if (!dq_wait_b(D)) return false;
         if (lane == 0) {
             mbar_arrive(&S->a_full[D.a.idx]);
             mbar_arrive(&S->raw_empty[D.raw.idx]);
@@ -572,6 +584,7 @@ __device__ bool dq_run_bf16(DqCtx &D, const StepGeo &G, int ks0, bool zero) {
         tc_wait_st();
         tc_fence_before();
         __syncwarp();
+        if (!dq_wait_b(D)) return false;
         if (lane == 0) {
             mbar_arrive_n(&S->raw_empty[slot], 4 * 32 / rps);   // four arrivals complete a slot
             mbar_arrive(&S->a_full[D.a.idx]);
@@ -597,9 +610,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
     if (tid == 0) {
         for (int i = 0; i < SR; ++i) { mbar_init(&S->raw_full[i], 1); mbar_init(&S->raw_empty[i], 4); }
         for (int i = 0; i < 2 * kGemmSS; ++i) { mbar_init(&S->sc_full[i], 1); mbar_init(&S->sc_empty[i], 4); }
-        // a_empty / b_empty / acc_full: one commit from each of the two MMA issuers
+        // a_empty / acc_full: one commit from each of the two MMA issuers
         for (int i = 0; i < kGemmSA; ++i) { mbar_init(&S->a_full[i], 4); mbar_init(&S->a_empty[i], 2); }
-        for (int i = 0; i < kGemmSB; ++i) { mbar_init(&S->b_full[i], 1); mbar_init(&S->b_empty[i], 2); }
+        for (int i = 0; i < kGemmSB; ++i) mbar_init(&S->b_full[i], 1);
         for (int i = 0; i < 2; ++i) { mbar_init(&S->acc_full[i], 2); mbar_init(&S->acc_empty[i], 4); }
         mbar_init(&S->drain[0], 1);
         mbar_init(&S->drain[1], 1);
@@ -702,7 +715,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
         // release; for single-matrix problems warp 3 only adds its arrivals.
         const int mat = warp == 1 ? 0 : 1;
         if (lane == 0) {
-            Ring a(kGemmSA), b(kGemmSB);
+            Ring a(kGemmSA);
             uint32_t tile = 0;
             bool issued = false, ok = true;
             for (int it = blockIdx.x; it < n_items && ok && !S->abort; it += gridDim.x, ++tile) {
@@ -717,22 +730,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
                 const uint32_t idesc = idesc_bf16((w.n + 15) & ~15);
                 const uint32_t d = tmem + ab * 128 + mat * 128;   // this issuer's accumulator
                 for (int s = 0; s < steps; ++s) {
-                    if (!mbar_wait_sleep(&S->b_full[b.idx], b.phase, deadline)) { ok = false; break; }
-                    if (mat == 0) trace_put(P, 8, a.count);
+                    // a_full: the A rows are in TMEM and the B tile has landed
                     if (!mbar_wait_sleep(&S->a_full[a.idx], a.phase, deadline)) { ok = false; break; }
                     tc_fence_after();
-                    if (mat == 0) trace_put(P, 4, a.count);
                     if (mine) {
-                        const uint64_t bd = sw128_desc(smem_u32(sB + b.idx * kGemmBStage));
+                        const uint64_t bd = sw128_desc(smem_u32(sB + a.idx * kGemmBStage));
                         const uint32_t a0 = tmem + kGemmAccCols + a.idx * kGemmACols + mat * 32;
 #pragma unroll
                         for (int kk = 0; kk < 4; ++kk) tc_mma_ts(d, a0 + 8 * kk, bd + 2 * kk, idesc, (s | kk) ? 1u : 0u);
                         issued = true;
                     }
-                    tc_commit(&S->a_empty[a.idx]);
-                    tc_commit(&S->b_empty[b.idx]);
+                    tc_commit(&S->a_empty[a.idx]);   // frees the A and the B stage
                     a.next();
-                    b.next();
                 }
                 if (!ok) break;
                 tc_commit(&S->acc_full[ab]);
@@ -757,7 +766,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
                 for (int ps = 0; ps < npass && ok; ++ps) {
                     const CUtensorMap *map = &pr.tx[gemm_pass(pr.passes, ps) == 1 ? 1 : 0];
                     for (int j = 0; j < G.kb; ++j) {
-                        if (!mbar_wait_sleep(&S->b_empty[b.idx], b.phase ^ 1, deadline) || S->abort) { ok = false; break; }
+                        if (!mbar_wait_sleep(&S->a_empty[b.idx], b.phase ^ 1, deadline) || S->abort) { ok = false; break; }
                         uint8_t *dst = sB + b.idx * kGemmBStage;
                         trace_put(P, 1, b.count);
                         mbar_arrive_expect_tx(&S->b_full[b.idx], nt * 2048);
