@@ -401,6 +401,29 @@ bool make_matrix_maps(BatchedState *B, GemmProblem &pr, int m, const uint8_t *ba
            make_map(B, &pr.tb[m], base + b_off, false, ng, s_row_stride, bands, band_stride, groups, group_stride, 8);
 }
 
+// The kernel instantiation for the problems of a launch (see k_moe_gemm's parameters).
+using GemmKernel = void (*)(const GemmParams);
+#define NMOE_GEMM_KINDS(X)                                                      \
+    X(kAFmtBf16, 1, 1, kAFmtBf16, 1, 1) X(kAFmtQ4, 1, 1, kAFmtQ4, 1, 1)           \
+    X(kAFmtQ4, 2, 0, kAFmtBf16, 2, 0) X(kAFmtQ4, 2, 0, kAFmtQ4, 2, 0)             \
+    X(kAFmtQ2, 2, 0, kAFmtBf16, 2, 0) X(kAFmtQ2, 2, 0, kAFmtQ4, 2, 0)             \
+    X(kAFmtQ4, 1, 0, kAFmtBf16, 1, 0) X(kAFmtQ4, 1, 0, kAFmtQ4, 1, 0)             \
+    X(kAFmtQ2, 1, 0, kAFmtBf16, 1, 0) X(kAFmtQ2, 1, 0, kAFmtQ4, 1, 0)
+
+GemmKernel gemm_kernel(const GemmParams &P) {
+    const GemmProblem &a = P.prob[0];
+    const GemmProblem &b = P.n_prob > 1 ? P.prob[1] : P.prob[0];
+    // a single problem reuses an instantiation whose second problem is never reached;
+    // with two problems the shared expert is bf16 or q4
+    const int bf = P.n_prob > 1 ? b.fmt : (a.split ? a.fmt : kAFmtBf16);
+#define NMOE_GEMM_PICK(f0, m0, s0, f1, m1, s1)                                                   \
+    if (a.fmt == f0 && a.n_mat == m0 && (a.split != 0) == (s0 != 0) && bf == f1)                 \
+        return k_moe_gemm<f0, m0, s0, f1, m1, s1>;
+    NMOE_GEMM_KINDS(NMOE_GEMM_PICK)
+#undef NMOE_GEMM_PICK
+    return nullptr;
+}
+
 cudaError_t launch_gemm(nmoe_moe_ctx *ctx, GemmParams &P, cudaStream_t st) {
     int sr = kGemmMaxSlots;
     while (sr > 2 && gemm_smem_bytes(sr) > (size_t)kGemmSmemMax) --sr;
@@ -413,7 +436,9 @@ cudaError_t launch_gemm(nmoe_moe_ctx *ctx, GemmParams &P, cudaStream_t st) {
     BatchedState *B = ctx->batched;
     P.trace = (B->trace && B->launch_no == B->trace_launch) ? B->trace : nullptr;
     ++B->launch_no;
-    k_moe_gemm<<<ctx->num_sms, kGemmThreads, gemm_smem_bytes(sr), st>>>(P);
+    const GemmKernel kern = gemm_kernel(P);
+    if (kern == nullptr) return cudaErrorInvalidValue;
+    kern<<<ctx->num_sms, kGemmThreads, gemm_smem_bytes(sr), st>>>(P);
     return cudaGetLastError();
 }
 
@@ -447,7 +472,13 @@ int nmoe_batched_init(nmoe_moe_ctx *ctx) {
         return NMOE_ECUDA;
     }
     B->encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-    cudaError_t e = cudaFuncSetAttribute(k_moe_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmemMax);
+    cudaError_t e = cudaSuccess;
+#define NMOE_GEMM_ATTR(f0, m0, s0, f1, m1, s1)                                                           \
+    if (e == cudaSuccess)                                                                                \
+        e = cudaFuncSetAttribute(k_moe_gemm<f0, m0, s0, f1, m1, s1>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                 kGemmSmemMax);
+    NMOE_GEMM_KINDS(NMOE_GEMM_ATTR)
+#undef NMOE_GEMM_ATTR
     if (e != cudaSuccess) {
         nmoe_ctx_set_error(ctx, "gemm smem attribute: %s", cudaGetErrorString(e));
         return NMOE_ECUDA;

@@ -595,6 +595,16 @@ __device__ bool dq_run_bf16(DqCtx &D, const StepGeo &G, int ks0, bool zero) {
     return true;
 }
 
+// One dequant pass of a problem whose (format, matrices, split) are compile-time: each
+// kernel instantiation carries only the conversion code its problems use.
+template <int kFmt, int kNMat, int kSplit>
+__device__ __forceinline__ bool dq_pass(DqCtx &D, const StepGeo &G, int ks0, bool lo) {
+    if constexpr (kFmt == kAFmtBf16) return dq_run_bf16<kNMat>(D, G, ks0, kSplit && lo);
+    else return dq_run_q<kFmt, kNMat, kSplit != 0>(D, G, ks0, lo);
+}
+
+// Template parameters: (format, matrices, split) of problem 0 and of problem 1.
+template <int F0, int M0, int S0, int F1, int M1, int S1>
 __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_constant__ GemmParams P) {
     extern __shared__ __align__(1024) uint8_t smraw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
@@ -803,17 +813,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
             const int npass = __popc(pr.passes), ks0 = w.sp * G.kb;
             for (int ps = 0; ps < npass && ok; ++ps) {
                 const bool lo = gemm_pass(pr.passes, ps) == 2;
-                if (pr.fmt == kAFmtBf16) {
-                    ok = pr.n_mat == 2 ? dq_run_bf16<2>(D, G, ks0, pr.split && lo) : dq_run_bf16<1>(D, G, ks0, pr.split && lo);
-                } else if (pr.fmt == kAFmtQ4) {
-                    ok = pr.split ? dq_run_q<kAFmtQ4, 1, true>(D, G, ks0, lo)
-                                  : pr.n_mat == 2 ? dq_run_q<kAFmtQ4, 2, false>(D, G, ks0, lo)
-                                                  : dq_run_q<kAFmtQ4, 1, false>(D, G, ks0, lo);
-                } else {
-                    ok = pr.split ? dq_run_q<kAFmtQ2, 1, true>(D, G, ks0, lo)
-                                  : pr.n_mat == 2 ? dq_run_q<kAFmtQ2, 2, false>(D, G, ks0, lo)
-                                                  : dq_run_q<kAFmtQ2, 1, false>(D, G, ks0, lo);
-                }
+                ok = w.p == 0 ? dq_pass<F0, M0, S0>(D, G, ks0, lo) : dq_pass<F1, M1, S1>(D, G, ks0, lo);
             }
         }
         if (!ok && lane == 0) gemm_fail(S, P.err);
