@@ -189,9 +189,9 @@ def run_reference(args, rank, world):
     from oracle import oracle as O
     O.build()
     n_layers = 2
-    layers, xs = build_workload(n_layers, 4, 8, 1, 1, pool=8, seed=args.seed)
+    layers, xs = build_workload(n_layers, args.bits, args.k, 1, 1, pool=8, seed=args.seed)
     calls_per_step = 4
-    k = 8
+    k = args.k
 
     def step():
         for j in range(calls_per_step):
@@ -205,14 +205,15 @@ def run_reference(args, rank, world):
     el = time.perf_counter() - t0
     value = args.steps * calls_per_step / el
     cores = O.lib().orc_get_threads()
-    sample = (f"{calls_per_step} batch-1 layer calls per step (config 0: q4 experts, k=8, bf16 router/shared), "
+    sample = (f"{calls_per_step} batch-1 layer calls per step (q{args.bits} experts, k={k}, bf16 router/shared), "
               f"CPU oracle port of the reference block, OpenMP over output rows")
     return {
         "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded bf16 ~N(0,0.02) weights quantised by the reference quantiser rule)",
-        "config": {"workload": "config0 batch-1 decode, q4 experts, k=8, bf16 router/shared, x bf16",
+        "config": {"workload": f"config{0 if args.bits == 4 else 1} batch-1 decode, q{args.bits} experts, k={k}, "
+                               "bf16 router/shared, x bf16",
                    "layers_in_sample": n_layers},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -408,7 +409,7 @@ def run_ours(args, rank, world, local_rank):
 
     dev = local_rank
     torch.cuda.set_device(dev)
-    bits, k, rdt, sdt = 4, 8, N.DTYPE_BF16, N.DTYPE_BF16
+    bits, k, rdt, sdt = args.bits, args.k, N.DTYPE_BF16, N.DTYPE_BF16
     L = args.layers
     layers, xs_h = build_workload(L, bits, k, rdt, sdt, pool=args.pool, seed=args.seed + rank)
     flags = N.FLAG_PREFETCH_NEXT_LAYER if args.prefetch else 0
@@ -520,11 +521,13 @@ def run_ours(args, rank, world, local_rank):
         result = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16/q4 in, f32 accumulate",
+            "scaling": "weak", "vs_baseline": None, "dtype": f"bf16/q{bits} in, f32 accumulate",
             "data": "synthetic (seeded bf16 ~N(0,0.02) weights quantised by the reference quantiser rule; "
                     f"{args.pool} distinct expert packs placed in 256 slots per layer)",
-            "config": {"workload": "config0 batch-1 decode: 40 layers x 256 q4 experts resident, k=8, "
-                                   "bf16 router/shared/gate-vector, x bf16 [1,2048]",
+            "config": {"workload": (f"config0 batch-1 decode: {L} layers x 256 q4 experts resident, k={k}, "
+                                    if bits == 4 else
+                                    f"config1 batch-1 decode: {L} layers x 256 q2 experts resident, k={k}, ")
+                                   + "bf16 router/shared/gate-vector, x bf16 [1,2048]",
                        "layers": L, "k": k, "step": f"{L} layer calls (one token through {L} MoE blocks)",
                        "l2": "inputs larger than L2 (a step touches ~860 MB of weights)",
                        "parallelism": "replicas only" if world > 1 else "single GPU",
@@ -532,7 +535,7 @@ def run_ours(args, rank, world, local_rank):
                        "next_layer_prefetch": bool(args.prefetch)},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk, "unit": "GB/s", "frac": achieved / pk,
                          "peak_kind": pk_kind, "algorithmic_bytes_per_launch": abytes,
-                         "traffic": profiled_traffic("decode_fused_cfg0")},
+                         "traffic": profiled_traffic("decode_fused_cfg0") if (bits, k) == (4, 8) else None},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": L * HIDDEN * 2,
                     "d2h_bytes_per_step": L * HIDDEN * 4},
@@ -558,6 +561,8 @@ def main():
     ap.add_argument("--seed", type=int, default=2026)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--workload", choices=["decode", "batched"], default="decode")
+    ap.add_argument("--bits", type=int, choices=[2, 4], default=4, help="decode: expert packs (4: config 0, 2: config 1)")
+    ap.add_argument("--k", type=int, default=8, help="decode: routed experts per token (config 1 sweeps 1..8)")
     ap.add_argument("--tokens", type=int, default=4096, help="T for --workload batched")
     ap.add_argument("--batched-layers", type=int, default=4, help="resident layers cycled by --workload batched")
     ap.add_argument("--prefetch", action="store_true",
