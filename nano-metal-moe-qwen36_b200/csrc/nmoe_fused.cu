@@ -364,16 +364,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
     const int nU = (32 * k > c) ? (32 * k - c + G - 1) / G : 0;
     const int nB = (128 > (G - 1 - c)) ? (128 - (G - 1 - c) + G - 1) / G : 0;   // bands b = G-1-c + i*G
     const int band0 = G - 1 - c;
-    uint32_t tag;
-    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(tag) : "l"(&sy->epoch) : "memory");
-    tag += 1u;
-    // residual rows this thread combines at the end: load early, latency hidden
-    float hm_reg = 0.f;
-    if (!P.route_only && P.h_mid && tid < nB * 16)   // volatile: keep the load here, not at its use
-        asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(hm_reg) : "l"(P.h_mid + (band0 + (tid >> 4) * G) * 16 + (tid & 15)));
-
+    // Programmatic dependent launch: the next call on this stream may start launching now;
+    // its CTAs become resident as this call's CTAs exit.
+    if (tid == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (tid == 0) {
-        if (P.timeline) sy->tl[c & 1023][0] = (uint32_t)t_start;
         for (int i = 0; i < kMaxBars; ++i) mbar_init(&bars[i], 1);
         mbar_fence_init();
         S->abort = 0;
@@ -384,16 +378,30 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
     }
     __syncthreads();
 
-    // ---- 0. routing-independent copies (x first: it gates everything) ------------------
+    // ---- 0. routing-independent copies ------------------------------------------------
+    // The router rows depend on nothing the previous call on this stream produces: they
+    // go out before the dependency wait. x, h_mid and the shared sync state (the epoch
+    // word and the exchange buffers) are read only after it.
     if (tid == 0) {
         const uint64_t pol = policy_evict_first();
-        const uint32_t xbytes = P.x_f32 ? kHidden * 4 : kHidden * 2;
-        mbar_arrive_expect_tx(&bars[kBarX], xbytes);
-        bulk_g2s(sm + Y.xraw, P.x, xbytes, &bars[kBarX], pol);
         mbar_arrive_expect_tx(&bars[kBarRouter], nR * RW);
         if (nR) bulk_g2s(sm + Y.rw, P.router + (size_t)r0 * RW, nR * RW, &bars[kBarRouter], pol);
         mbar_arrive_expect_tx(&bars[kBarShared], nS * SPW + (has_gvec ? SRW : 0));
         mbar_arrive_expect_tx(&bars[kBarSDown], P.route_only ? 0u : nB * 16 * SDW);
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    uint32_t tag;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(tag) : "l"(&sy->epoch) : "memory");
+    tag += 1u;
+    // residual rows this thread combines at the end: load early, latency hidden
+    float hm_reg = 0.f;
+    if (!P.route_only && P.h_mid && tid < nB * 16)   // volatile: keep the load here, not at its use
+        asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(hm_reg) : "l"(P.h_mid + (band0 + (tid >> 4) * G) * 16 + (tid & 15)));
+    if (tid == 0) {
+        if (P.timeline) sy->tl[c & 1023][0] = (uint32_t)t_start;
+        const uint32_t xbytes = P.x_f32 ? kHidden * 4 : kHidden * 2;
+        mbar_arrive_expect_tx(&bars[kBarX], xbytes);
+        bulk_g2s(sm + Y.xraw, P.x, xbytes, &bars[kBarX], policy_evict_first());
     }
     // The shared-expert copies go out only once the router rows have landed (see phase
     // 2), so that the router bytes do not queue behind them in this SM's copy engine.
@@ -904,6 +912,7 @@ struct nmoe::FusedState {
     uint64_t timeout_ns = 1000000000ull;
     int timeline = 0;
     int shared_early = 1;
+    int pdl = 1;   // launch with programmatic dependent launch (NMOE_PDL=0 turns it off)
     int expert_fp32 = 0;   // NMOE_EXPERT_FP32=1: fp32 routed-expert dots (slower, ~1e-6)
 };
 
@@ -976,6 +985,7 @@ int nmoe_fused_init(nmoe_moe_ctx *ctx) {
     if (const char *t = getenv("NMOE_WAIT_TIMEOUT_MS")) F->timeout_ns = (uint64_t)atoll(t) * 1000000ull;
     if (const char *t = getenv("NMOE_TIMELINE")) F->timeline = atoi(t) != 0;
     if (const char *t = getenv("NMOE_SHARED_EARLY")) F->shared_early = atoi(t) != 0;
+    if (const char *t = getenv("NMOE_PDL")) F->pdl = atoi(t) != 0;
     F->expert_fp32 = (ctx->cfg.flags & NMOE_FLAG_EXPERT_FP32) != 0;
     if (const char *t = getenv("NMOE_EXPERT_FP32")) F->expert_fp32 = atoi(t) != 0;
     const int bits = ctx->cfg.quant_bits;
@@ -1008,17 +1018,19 @@ void nmoe_fused_destroy(nmoe_moe_ctx *ctx) {
 }
 
 template <int kBits, bool kRQ4, bool kSQ4>
-static cudaError_t launch(const FusedParams &p, int grid, cudaStream_t st, bool half) {
+static cudaError_t launch(const FusedParams &p, int grid, cudaStream_t st, bool half, bool pdl) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = p.lay.total;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeCooperative;
     attr[0].val.cooperative = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl ? 2 : 1;
     if (half) return cudaLaunchKernelEx(&cfg, k_moe_decode_fused<kBits, kRQ4, kSQ4, true>, p);
     return cudaLaunchKernelEx(&cfg, k_moe_decode_fused<kBits, kRQ4, kSQ4, false>, p);
 }
@@ -1052,7 +1064,7 @@ cudaError_t nmoe_fused_launch(nmoe_moe_ctx *ctx, const FusedCall &a, cudaStream_
     const int bits = ctx->cfg.quant_bits;
     const bool rq4 = ctx->cfg.router_dtype == NMOE_DTYPE_Q4, sq4 = ctx->cfg.shared_dtype == NMOE_DTYPE_Q4;
 #define NMOE_L(B, R, S) \
-    if (bits == B && rq4 == R && sq4 == S) return launch<B, R, S>(p, F->grid, st, !F->expert_fp32);
+    if (bits == B && rq4 == R && sq4 == S) return launch<B, R, S>(p, F->grid, st, !F->expert_fp32, F->pdl);
     NMOE_L(4, false, false) NMOE_L(4, true, false) NMOE_L(4, false, true) NMOE_L(4, true, true)
     NMOE_L(2, false, false) NMOE_L(2, true, false) NMOE_L(2, false, true) NMOE_L(2, true, true)
 #undef NMOE_L
