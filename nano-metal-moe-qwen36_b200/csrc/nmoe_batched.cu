@@ -614,7 +614,9 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
     else cudaMemsetAsync(B->cnt, 0, kExperts * sizeof(int), st);
 
     // K slices of the dense problems (router, shared gate/up, shared down)
-    const int target = ctx->num_sms;
+    // a quarter of the SMs' worth of items: more K slices leave each item a step or two and
+    // the consumers (k_route, k_shared_act, k_combine) more partials to add (measured)
+    const int target = ctx->num_sms / 4;
     const int nsplit_r = pick_ksplit(rfmt, 1, kHidden, 2, T, B->rows_cap, target);
     const int nsplit_g = pick_ksplit(sfmt, 2, kHidden, 4, T, B->rows_cap, target);
     const int nsplit_d = pick_ksplit(sfmt, 1, kInter, 16, T, B->rows_cap, target);
