@@ -47,8 +47,8 @@ constexpr int kGemmMaxGroups = 256;
 constexpr int kGemmMaxProblems = 2;
 constexpr int kGemmSA = 4, kGemmSB = kGemmSA, kGemmSS = 2;   // kGemmSS scale stages per dequant group
 // A step's A stage (TMEM) and B stage (shared memory) share one ring position: one MMA
-// commit frees both, and the dequant warps wait for the B tile before they mark the step
-// ready, so the MMA issuer waits on a single barrier per step.
+// commit frees both, and the B tile's TMA completes on the stage's a_full barrier, so the
+// MMA issuer waits on a single barrier per step.
 constexpr int kGemmMaxSlots = 16;
 constexpr uint32_t kGemmAccCols = 256; // accumulators: TMEM columns [0, 256)
 constexpr uint32_t kGemmACols = 64;    // one A stage: 2 matrices x 32 columns (bf16 pairs)
@@ -430,7 +430,6 @@ struct GemmSmem {
     uint64_t raw_full[kGemmMaxSlots], raw_empty[kGemmMaxSlots];
     uint64_t sc_full[2 * kGemmSS], sc_empty[2 * kGemmSS];   // [group][stage]
     uint64_t a_full[kGemmSA], a_empty[kGemmSA];
-    uint64_t b_full[kGemmSB];
     uint64_t acc_full[2], acc_empty[2];
     uint64_t drain[2];
     uint32_t tmem_base;
@@ -494,12 +493,15 @@ __device__ __forceinline__ void dq_trace(const DqCtx &D, int row, uint32_t i) {
     }
 }
 
-// The step's B tile has landed (lane 0 waits; the warp agrees).
-__device__ __forceinline__ bool dq_wait_b(const DqCtx &D) {
+// The step's A stage is free (the MMAs that read it have completed): lane 0 waits, the
+// warp follows it.
+__device__ __forceinline__ bool dq_wait_a_free(const DqCtx &D) {
     const int lane = threadIdx.x & 31;
     bool ok = true;
-    if (lane == 0) ok = mbar_wait_sleep(&D.S->b_full[D.a.idx], D.a.phase, D.deadline);
-    return __all_sync(0xffffffffu, ok);
+    if (lane == 0) ok = mbar_wait_sleep(&D.S->a_empty[D.a.idx], D.a.phase ^ 1, D.deadline);
+    ok = __all_sync(0xffffffffu, ok);
+    tc_fence_after();
+    return ok;
 }
 
 // One pass over the steps [ks0, ks0 + kb) of an item, q4/q2 weights.
@@ -516,8 +518,7 @@ __device__ bool dq_run_q(DqCtx &D, const StepGeo &G, int ks0, bool lo) {
         }
         const int ks = ks0 + j;
         dq_trace(D, 10, D.a.count);
-        if (!__all_sync(0xffffffffu, mbar_wait_sleep(&S->a_empty[D.a.idx], D.a.phase ^ 1, D.deadline))) return false;
-        tc_fence_after();
+        if (!dq_wait_a_free(D)) return false;
         dq_trace(D, 11, D.a.count);
         const int si = D.grp * kGemmSS + D.sc.idx;
         if ((ks >> 3) != lastw) {
@@ -542,7 +543,6 @@ __device__ bool dq_run_q(DqCtx &D, const StepGeo &G, int ks0, bool lo) {
         // last step of this group in the scale window: the group's next step is 2 on
         const bool rel_sc = ((ks + 2) >> 3) != (ks >> 3) || j + 2 >= G.kb;
         dq_trace(D, 3, D.a.count);
-        if (!dq_wait_b(D)) return false;
         if (lane == 0) {
             mbar_arrive(&S->a_full[D.a.idx]);
             mbar_arrive(&S->raw_empty[D.raw.idx]);
@@ -571,8 +571,7 @@ __device__ bool dq_run_bf16(DqCtx &D, const StepGeo &G, int ks0, bool zero) {
             D.a.next();
             continue;
         }
-        if (!__all_sync(0xffffffffu, mbar_wait_sleep(&S->a_empty[D.a.idx], D.a.phase ^ 1, D.deadline))) return false;
-        tc_fence_after();
+        if (!dq_wait_a_free(D)) return false;
         const uint32_t slot = D.raw.idx + qs < (uint32_t)D.SR ? D.raw.idx + qs : D.raw.idx + qs - D.SR;
         const uint32_t ph = D.raw.idx + qs < (uint32_t)D.SR ? D.raw.phase : D.raw.phase ^ 1;
         if (!__all_sync(0xffffffffu, mbar_wait_sleep(&S->raw_full[slot], ph, D.deadline))) return false;
@@ -584,7 +583,6 @@ __device__ bool dq_run_bf16(DqCtx &D, const StepGeo &G, int ks0, bool zero) {
         tc_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (!dq_wait_b(D)) return false;
         if (lane == 0) {
             mbar_arrive_n(&S->raw_empty[slot], 4 * 32 / rps);   // four arrivals complete a slot
             mbar_arrive(&S->a_full[D.a.idx]);
@@ -621,8 +619,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
         for (int i = 0; i < SR; ++i) { mbar_init(&S->raw_full[i], 1); mbar_init(&S->raw_empty[i], 4); }
         for (int i = 0; i < 2 * kGemmSS; ++i) { mbar_init(&S->sc_full[i], 1); mbar_init(&S->sc_empty[i], 4); }
         // a_empty / acc_full: one commit from each of the two MMA issuers
-        for (int i = 0; i < kGemmSA; ++i) { mbar_init(&S->a_full[i], 4); mbar_init(&S->a_empty[i], 2); }
-        for (int i = 0; i < kGemmSB; ++i) mbar_init(&S->b_full[i], 1);
+        // a_full: four dequant warps + the B loader's expect_tx (its TMA tiles complete on
+        // the same barrier), so a full stage has its A rows in TMEM and its B tile landed
+        for (int i = 0; i < kGemmSA; ++i) { mbar_init(&S->a_full[i], 5); mbar_init(&S->a_empty[i], 2); }
         for (int i = 0; i < 2; ++i) { mbar_init(&S->acc_full[i], 2); mbar_init(&S->acc_empty[i], 4); }
         mbar_init(&S->drain[0], 1);
         mbar_init(&S->drain[1], 1);
@@ -779,15 +778,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
                         if (!mbar_wait_sleep(&S->a_empty[b.idx], b.phase ^ 1, deadline) || S->abort) { ok = false; break; }
                         uint8_t *dst = sB + b.idx * kGemmBStage;
                         trace_put(P, 1, b.count);
-                        mbar_arrive_expect_tx(&S->b_full[b.idx], nt * 2048);
+                        mbar_arrive_expect_tx(&S->a_full[b.idx], nt * 2048);
                         for (int i = 0; i < nt; ++i)
-                            tma_load_2d(dst + i * 2048, map, (ks0 + j) * 64, row0 + 16 * i, &S->b_full[b.idx]);
+                            tma_load_2d(dst + i * 2048, map, (ks0 + j) * 64, row0 + 16 * i, &S->a_full[b.idx]);
                         b.next();
                     }
                 }
             }
             if (!ok) gemm_fail(S, P.err);
-            b.drain(S->b_full, deadline);
+            b.drain(S->a_full, deadline);
         }
     } else if (warp < 12) {
         // ------------------------------------------------ dequant (2 x 128 threads) ----
