@@ -83,7 +83,7 @@ struct FusedParams {
     uint32_t *idx_out;
     float *w_out;
     float *logits_out;
-    int k, num_experts, route_only, timeline, shared_early;
+    int k, num_experts, route_only, timeline;
     FusedSync *sy;
     int *err;
     FusedLayout lay;
@@ -181,7 +181,9 @@ __device__ __forceinline__ void load_x8(const float *xs, int c8, float *xr) {
 template <bool kQ4, int NR>
 __device__ __forceinline__ void dense_dot(const uint8_t *const *w, const uint16_t *const *s, const uint16_t *const *b,
                                           const float *xs, const float *xsum, int c0, int cstep, int c1, float *acc) {
+    // one or two trips per lane at the kernel's shapes: no unrolling (code size is latency)
     if (kQ4) {
+#pragma unroll 1
         for (int c = c0; c < c1; c += cstep) {
             float xr[32];
             load_x32(xs, c, xr);
@@ -193,6 +195,7 @@ __device__ __forceinline__ void dense_dot(const uint8_t *const *w, const uint16_
             }
         }
     } else {
+#pragma unroll 1
         for (int c = c0; c < c1; c += cstep) {
             float xr[8];
             load_x8(xs, c, xr);
@@ -414,7 +417,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
                 bulk_g2s(sm + Y.sdn + i * 16 * SDW, P.sdown + (size_t)(band0 + i * G) * 16 * SDW, 16 * SDW,
                          &bars[kBarSDown], pol);
     };
-    if (tid == 0 && P.shared_early && nR == 0) issue_shared();
+    if (tid == 0 && nR == 0) issue_shared();
     // The routed down bands are only needed after the act exchange: they go out once this
     // CTA's first gate/up unit has landed, so that the gate/up bytes are not interleaved
     // with them in HBM.
@@ -480,7 +483,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
             if (u < uR) {
                 if (!r_ready) {
                     if (!(r_ready = mbar_wait_warp(&bars[kBarRouter], 0, deadline))) return false;
-                    if (P.shared_early && u == 0 && lane == 0) issue_shared();
+                    if (u == 0 && lane == 0) issue_shared();
                 }
                 const int row = u / kSeg, seg = u % kSeg, len = kRChunks / kSeg;
                 const uint8_t *base = sm + Y.rw + row * RW;
@@ -554,12 +557,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
             return true;
         };
     {
-        // warp 0 takes router units only (it runs the top-k next); with early shared
-        // copies the shared units go to warps 1..15 now, otherwise after the routed gate/up
+        // warp 0 takes router units only (it runs the top-k next); the shared units go to
+        // warps 1..15 once their router units are done. One loop, so that the unit code is
+        // emitted once: the kernel's serial path is sensitive to instruction-fetch misses.
         bool ok = !S->abort;
-        for (int u = warp; ok && u < uR; u += kWarps) ok = do_unit(u);
-        if (P.shared_early && warp != 0)
-            for (int v = warp - 1; ok && v < uS + uG; v += kWarps - 1) ok = do_unit(uR + v);
+        const int uEnd = warp == 0 ? uR : uR + uS + uG;
+        for (int u = warp < uR ? warp : (warp == 0 ? uEnd : uR + warp - 1); ok && u < uEnd;) {
+            ok = do_unit(u);
+            if (u < uR) {
+                u += kWarps;
+                if (u >= uR && warp != 0) u = uR + warp - 1;   // first shared unit of this warp
+            } else {
+                u += kWarps - 1;
+            }
+        }
         if (!ok && lane == 0) NMOE_GIVEUP(2);
     }
 
@@ -567,6 +578,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
     if (kHalf && warp != 0) {
         const int E = half_exp(__uint_as_float(S->xmax_bits));
         __half2 *xh = reinterpret_cast<__half2 *>(sm + Y.xh);
+#pragma unroll 1
         for (int e = tid - 32; e < 1024; e += kThreads - 32) xh[e] = pair_entry<kBits>(xs, e, E);
     }
     NMOE_PHASE(2);
@@ -627,7 +639,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
                     mbar_arrive_expect_tx(&bars[kBarBand0 + i], bytes);
                 }
                 if (nU == 0) issue_bands();
-                if (!P.shared_early) issue_shared();
                 NMOE_STAMP(10);
             }
         }
@@ -708,12 +719,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
             __threadfence();
             asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(&sy->uflag[c + tid * G]), "r"(tag) : "memory");
         }
-        if (!P.shared_early) {
-            bool ok = true;
-            for (int v = warp; ok && v < uS + uG; v += kWarps) ok = do_unit(uR + v);
-            if (!ok && lane == 0) NMOE_GIVEUP(2);
-            __syncthreads();
-        }
         NMOE_PHASE(4);
 
         // ---- 5. output bands: shared down + k expert downs + combine -----------------
@@ -748,6 +753,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
             if (!S->abort) {
                 // shared down: warp per output row (16 rows per band)
                 if (mbar_wait_warp(&bars[kBarSDown], 0, deadline)) {
+#pragma unroll 1
                     for (int rr = warp; rr < nB * 16; rr += kWarps) {
                         const uint8_t *base = sm + Y.sdn + rr * SDW;
                         const uint8_t *w[1] = {base};
@@ -777,6 +783,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
                     if (!got) NMOE_GIVEUP(6);
                 }
                 __syncthreads();
+#pragma unroll 1
                 for (int i0 = 0; i0 < k * kInter / 4; i0 += kThreads) {
                     const int i = i0 + tid;
                     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -806,6 +813,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
                 __syncthreads();
                 if (kHalf) {
                     __half2 *ah = reinterpret_cast<__half2 *>(sm + Y.acth);   // [k][256]
+#pragma unroll 1
                     for (int e = tid; e < k * 256; e += kThreads) {
                         const int sl = e >> 8;
                         ah[e] = pair_entry<kBits>(actf + sl * (kInter / 32) * kXP, e & 255,
@@ -911,7 +919,6 @@ struct nmoe::FusedState {
     bool ok = false;
     uint64_t timeout_ns = 1000000000ull;
     int timeline = 0;
-    int shared_early = 1;
     int pdl = 1;   // launch with programmatic dependent launch (NMOE_PDL=0 turns it off)
     int expert_fp32 = 0;   // NMOE_EXPERT_FP32=1: fp32 routed-expert dots (slower, ~1e-6)
 };
@@ -984,7 +991,6 @@ int nmoe_fused_init(nmoe_moe_ctx *ctx) {
     F->grid = ctx->num_sms;
     if (const char *t = getenv("NMOE_WAIT_TIMEOUT_MS")) F->timeout_ns = (uint64_t)atoll(t) * 1000000ull;
     if (const char *t = getenv("NMOE_TIMELINE")) F->timeline = atoi(t) != 0;
-    if (const char *t = getenv("NMOE_SHARED_EARLY")) F->shared_early = atoi(t) != 0;
     if (const char *t = getenv("NMOE_PDL")) F->pdl = atoi(t) != 0;
     F->expert_fp32 = (ctx->cfg.flags & NMOE_FLAG_EXPERT_FP32) != 0;
     if (const char *t = getenv("NMOE_EXPERT_FP32")) F->expert_fp32 = atoi(t) != 0;
@@ -1053,7 +1059,6 @@ cudaError_t nmoe_fused_launch(nmoe_moe_ctx *ctx, const FusedCall &a, cudaStream_
     p.k = a.k;
     p.num_experts = a.num_experts;
     p.route_only = a.route_only;
-    p.shared_early = F->shared_early;
     p.next_dense = a.next_dense;
     p.next_dense_bytes = a.next_dense_bytes;
     p.timeline = F->timeline;

@@ -8,63 +8,52 @@
 namespace nmoe {
 
 struct TopkScratch {
-    __align__(16) float cval[kExperts + 4];
-    __align__(16) int cidx[kExperts + 4];
     uint32_t idx[kMaxK];
     float sel_v[kMaxK];
 };
 
+// Order-preserving key of a float: unsigned comparison of keys is float comparison
+// (-0 and +0 map to one key, as they compare equal).
+__device__ __forceinline__ uint32_t topk_key(float f) {
+    const uint32_t u = __float_as_uint(f + 0.0f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float topk_val(uint32_t key) {
+    return __uint_as_float((key & 0x80000000u) ? (key & 0x7fffffffu) : ~key);
+}
+
 // Top-k of the 256 logits held 8 per lane (lane l: experts 8l..8l+7), one warp.
 // Rule of nmoe_cpu_topk (src/math.m:95-132) on the logits: descending, lower expert id
 // first on ties. Writes S->idx[0..k) and S->sel_v[0..k) (the selected logits).
-// Candidates are the logits >= min over 8 groups (4 lanes, 32 logits) of the group
-// maximum -- at least 8 logits qualify, so the top-k (k <= 8) are among them -- ranked
-// against each other.
+// Each lane keeps the best of its remaining logits (first position on ties); a round is
+// one warp max of those heads, and the lowest lane holding it -- the lowest expert id --
+// gives up its head. Registers only, k rounds of a few instructions: the routing sits
+// on the decode kernel's serial path, where every instruction is a fetch.
 __device__ __forceinline__ void warp_topk(const float *v, int k, TopkScratch *S, int lane) {
-    float m = v[0];
+    uint32_t key[8];
 #pragma unroll
-    for (int i = 1; i < 8; ++i) m = fmaxf(m, v[i]);
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-    float thr = m;
-    thr = fminf(thr, __shfl_xor_sync(0xffffffffu, thr, 4));
-    thr = fminf(thr, __shfl_xor_sync(0xffffffffu, thr, 8));
-    thr = fminf(thr, __shfl_xor_sync(0xffffffffu, thr, 16));
-    // candidate positions from 8 ballots (value slot j major, lane minor)
-    const uint32_t lt = (1u << lane) - 1u;
-    int base = 0;
+    for (int j = 0; j < 8; ++j) key[j] = topk_key(v[j]);
+    auto head = [&](uint32_t &hk, int &hj) {
+        hk = key[0];
+        hj = 0;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const bool cand = !(v[j] < thr);
-        const uint32_t b = __ballot_sync(0xffffffffu, cand);
-        if (cand) {
-            S->cval[base + __popc(b & lt)] = v[j];
-            S->cidx[base + __popc(b & lt)] = 8 * lane + j;
-        }
-        base += __popc(b);
-    }
-    const int nc = base;
-    const int ncp = (nc + 3) & ~3;   // pad to a multiple of 4 with entries that never win
-    if (lane < ncp - nc) {
-        S->cval[nc + lane] = -INFINITY;
-        S->cidx[nc + lane] = 1 << 20;
-    }
-    __syncwarp();
-    for (int q = lane; q < nc; q += 32) {
-        const float vi = S->cval[q];
-        const int ii = S->cidx[q];
-        int rank = 0;
-        for (int j = 0; j < ncp; j += 4) {
-            const float4 u = *reinterpret_cast<const float4 *>(&S->cval[j]);
-            const int4 ui = *reinterpret_cast<const int4 *>(&S->cidx[j]);
-            rank += (u.x > vi) | ((u.x == vi) & (ui.x < ii));
-            rank += (u.y > vi) | ((u.y == vi) & (ui.y < ii));
-            rank += (u.z > vi) | ((u.z == vi) & (ui.z < ii));
-            rank += (u.w > vi) | ((u.w == vi) & (ui.w < ii));
-        }
-        if (rank < k) {
-            S->idx[rank] = (uint32_t)ii;
-            S->sel_v[rank] = vi;
+        for (int j = 1; j < 8; ++j)
+            if (key[j] > hk) { hk = key[j]; hj = j; }
+    };
+    uint32_t hk;
+    int hj;
+    head(hk, hj);
+#pragma unroll 1
+    for (int r = 0; r < k; ++r) {
+        const uint32_t m = __reduce_max_sync(0xffffffffu, hk);
+        const int w = __ffs(__ballot_sync(0xffffffffu, hk == m)) - 1;
+        if (lane == w) {
+            S->idx[r] = (uint32_t)(8 * lane + hj);
+            S->sel_v[r] = topk_val(m);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (j == hj) key[j] = 0u;   // below every finite key: never picked again
+            head(hk, hj);
         }
     }
     __syncwarp();
