@@ -84,6 +84,7 @@ struct FusedParams {
     float *w_out;
     float *logits_out;
     int k, num_experts, route_only, timeline;
+    int stall;   // test hook: the logits poll waits for a tag that is never written
     FusedSync *sy;
     int *err;
     FusedLayout lay;
@@ -99,7 +100,7 @@ struct Ctl {
     float w[kMaxK];
     int valid[kMaxK];
     float score;
-    TopkScratch tk;
+
 };
 
 __device__ __forceinline__ void st_tagged(uint64_t *p, float v, uint32_t tag) {
@@ -590,9 +591,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
         bool ok = !S->abort;
         // wait on one word per lane first (light polling), then read the lane's 8 words
         float probe;
-        if (ok) ok = poll_tagged1(&sy->logits[8 * lane + 7], tag, &probe, deadline) &&
-                     poll_tagged4(&sy->logits[8 * lane], tag, v, deadline) &&
-                     poll_tagged4(&sy->logits[8 * lane + 4], tag, v + 4, deadline);
+        const uint32_t want = P.stall ? tag + 1u : tag;
+        if (ok) ok = poll_tagged1(&sy->logits[8 * lane + 7], want, &probe, deadline) &&
+                     poll_tagged4(&sy->logits[8 * lane], want, v, deadline) &&
+                     poll_tagged4(&sy->logits[8 * lane + 4], want, v + 4, deadline);
         ok = __all_sync(0xffffffffu, ok);
         if (lane == 0) NMOE_STAMP(15);
         if (!ok) {
@@ -602,15 +604,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
                 reinterpret_cast<float4 *>(P.logits_out)[2 * lane] = make_float4(v[0], v[1], v[2], v[3]);
                 reinterpret_cast<float4 *>(P.logits_out)[2 * lane + 1] = make_float4(v[4], v[5], v[6], v[7]);
             }
-            warp_topk(v, k, &S->tk, lane);
+            const TopkLane tk = warp_topk_lane(v, k, lane);
+            // renormalised weight of selection s (lane s): exp(l_s - l_0) / sum_t exp(l_t - l_0),
+            // the sum taken in selection order
+            const float ex = lane < k ? expf(tk.val - tk.l0) : 0.f;
+            float sum = 0.f;
+#pragma unroll 1
+            for (int t = 0; t < k; ++t) sum += __shfl_sync(0xffffffffu, ex, t);
             if (lane < kMaxK) {
                 const int s = lane;
-                const float l0 = S->tk.sel_v[0];
-                float sum = 0.f;
-                for (int t = 0; t < k; ++t) sum += expf(S->tk.sel_v[t] - l0);
-                const uint32_t e = s < k ? S->tk.idx[s] : 0u;
+                const uint32_t e = s < k ? tk.idx : 0u;
                 S->idx[s] = e;
-                const float w = s < k ? expf(S->tk.sel_v[s] - l0) / sum : 0.f;
+                const float w = s < k ? ex / sum : 0.f;
                 const int valid = s < k && e < (uint32_t)P.num_experts;
                 if (s < k && !valid) set_err(P.err, kErrExpertRange);
                 S->valid[s] = valid;
@@ -919,6 +924,7 @@ struct nmoe::FusedState {
     bool ok = false;
     uint64_t timeout_ns = 1000000000ull;
     int timeline = 0;
+    int stall = 0;   // NMOE_TEST_STALL_WAIT=1 (tests): one cross-CTA wait can never complete
     int pdl = 1;   // launch with programmatic dependent launch (NMOE_PDL=0 turns it off)
     int expert_fp32 = 0;   // NMOE_EXPERT_FP32=1: fp32 routed-expert dots (slower, ~1e-6)
 };
@@ -992,6 +998,7 @@ int nmoe_fused_init(nmoe_moe_ctx *ctx) {
     if (const char *t = getenv("NMOE_WAIT_TIMEOUT_MS")) F->timeout_ns = (uint64_t)atoll(t) * 1000000ull;
     if (const char *t = getenv("NMOE_TIMELINE")) F->timeline = atoi(t) != 0;
     if (const char *t = getenv("NMOE_PDL")) F->pdl = atoi(t) != 0;
+    if (const char *t = getenv("NMOE_TEST_STALL_WAIT")) F->stall = atoi(t) != 0;
     F->expert_fp32 = (ctx->cfg.flags & NMOE_FLAG_EXPERT_FP32) != 0;
     if (const char *t = getenv("NMOE_EXPERT_FP32")) F->expert_fp32 = atoi(t) != 0;
     const int bits = ctx->cfg.quant_bits;
@@ -1062,6 +1069,7 @@ cudaError_t nmoe_fused_launch(nmoe_moe_ctx *ctx, const FusedCall &a, cudaStream_
     p.next_dense = a.next_dense;
     p.next_dense_bytes = a.next_dense_bytes;
     p.timeline = F->timeline;
+    p.stall = F->stall;
     p.sy = F->sy;
     p.err = a.err;
     p.lay = F->lay;

@@ -24,37 +24,62 @@ __device__ __forceinline__ float topk_val(uint32_t key) {
 
 // Top-k of the 256 logits held 8 per lane (lane l: experts 8l..8l+7), one warp.
 // Rule of nmoe_cpu_topk (src/math.m:95-132) on the logits: descending, lower expert id
-// first on ties. Writes S->idx[0..k) and S->sel_v[0..k) (the selected logits).
-// Each lane keeps the best of its remaining logits (first position on ties); a round is
-// one warp max of those heads, and the lowest lane holding it -- the lowest expert id --
-// gives up its head. Registers only, k rounds of a few instructions: the routing sits
-// on the decode kernel's serial path, where every instruction is a fetch.
-__device__ __forceinline__ void warp_topk(const float *v, int k, TopkScratch *S, int lane) {
-    uint32_t key[8];
+// first on ties. Each lane sorts its 8 logits once (stable odd-even transposition: ties
+// keep the lower position first); a round is one warp max of the lanes' heads, and the
+// lowest lane holding it -- the lowest expert id -- pops its head. Registers only, one
+// short dependency chain per round. Lane r < k returns the r-th selection; every lane
+// returns the largest logit (l0).
+struct TopkLane {
+    uint32_t idx;
+    float val, l0;
+};
+__device__ __forceinline__ TopkLane warp_topk_lane(const float *v, int k, int lane) {
+    uint32_t key[8], id[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) key[j] = topk_key(v[j]);
-    auto head = [&](uint32_t &hk, int &hj) {
-        hk = key[0];
-        hj = 0;
+    for (int j = 0; j < 8; ++j) {
+        key[j] = topk_key(v[j]);
+        id[j] = (uint32_t)(8 * lane + j);
+    }
 #pragma unroll
-        for (int j = 1; j < 8; ++j)
-            if (key[j] > hk) { hk = key[j]; hj = j; }
-    };
-    uint32_t hk;
-    int hj;
-    head(hk, hj);
+    for (int ph = 0; ph < 8; ++ph)
+#pragma unroll
+        for (int j = ph & 1; j + 1 < 8; j += 2) {
+            const bool sw = key[j + 1] > key[j];
+            const uint32_t ka = key[j], kb = key[j + 1], ia = id[j], ib = id[j + 1];
+            key[j] = sw ? kb : ka;
+            key[j + 1] = sw ? ka : kb;
+            id[j] = sw ? ib : ia;
+            id[j + 1] = sw ? ia : ib;
+        }
+    TopkLane out{0u, 0.f, 0.f};
 #pragma unroll 1
     for (int r = 0; r < k; ++r) {
-        const uint32_t m = __reduce_max_sync(0xffffffffu, hk);
-        const int w = __ffs(__ballot_sync(0xffffffffu, hk == m)) - 1;
-        if (lane == w) {
-            S->idx[r] = (uint32_t)(8 * lane + hj);
-            S->sel_v[r] = topk_val(m);
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-                if (j == hj) key[j] = 0u;   // below every finite key: never picked again
-            head(hk, hj);
+        const uint32_t m = __reduce_max_sync(0xffffffffu, key[0]);
+        const int w = __ffs(__ballot_sync(0xffffffffu, key[0] == m)) - 1;
+        const uint32_t wid = __shfl_sync(0xffffffffu, id[0], w);
+        const float mv = topk_val(m);
+        if (r == 0) out.l0 = mv;
+        if (lane == r) {
+            out.idx = wid;
+            out.val = mv;
         }
+        const bool me = lane == w;   // pop the head; 0 is below every finite key
+#pragma unroll
+        for (int j = 0; j < 7; ++j) {
+            key[j] = me ? key[j + 1] : key[j];
+            id[j] = me ? id[j + 1] : id[j];
+        }
+        key[7] = me ? 0u : key[7];
+    }
+    return out;
+}
+
+// Same selection, written to S->idx[0..k) and S->sel_v[0..k).
+__device__ __forceinline__ void warp_topk(const float *v, int k, TopkScratch *S, int lane) {
+    const TopkLane t = warp_topk_lane(v, k, lane);
+    if (lane < k) {
+        S->idx[lane] = t.idx;
+        S->sel_v[lane] = t.val;
     }
     __syncwarp();
 }

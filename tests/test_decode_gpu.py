@@ -212,12 +212,15 @@ def test_repeated_calls_are_identical_and_counters_reset():
 
 
 def test_bounded_wait_timeout_reports_and_recovers(monkeypatch):
-    """A zero wait budget makes the kernel's cross-CTA waits expire: the call returns, the
-    host reads NMOE_ETIMEOUT from the device error word, and the device stays usable."""
+    """The logits wait is pointed at a tag that no CTA writes (NMOE_TEST_STALL_WAIT) with a
+    1 ms budget: the bounded wait expires, the call returns, the host reads NMOE_ETIMEOUT
+    from the device error word, and the device stays usable."""
     lw = O.make_layer(77, bits=4, distinct_experts=8)
-    monkeypatch.setenv("NMOE_WAIT_TIMEOUT_MS", "0")
+    monkeypatch.setenv("NMOE_WAIT_TIMEOUT_MS", "1")
+    monkeypatch.setenv("NMOE_TEST_STALL_WAIT", "1")
     ct = N.Context(quant_bits=4, num_layers=1, device=0)
     monkeypatch.delenv("NMOE_WAIT_TIMEOUT_MS")
+    monkeypatch.delenv("NMOE_TEST_STALL_WAIT")
     upload(ct, 0, lw)
     x, xd = make_x(8, N.DTYPE_BF16)
     out = torch.zeros(2048, dtype=torch.float32, device="cuda")
