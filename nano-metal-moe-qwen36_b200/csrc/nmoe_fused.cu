@@ -776,69 +776,71 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
             }
             __syncthreads();
             if (!S->abort) {
-                // act: wait for the 32k unit flags, then stage fp32 padded + parity sums
+                // act, slot by slot: the wps warps of slot s wait for that slot's 32 unit
+                // flags, stage its act (fp32 padded + parity sums) and its half2 pair table,
+                // then run its down dots. Slots are ready at different times (first units
+                // before second units), so no slot waits for the others; the group syncs on
+                // its own named barrier.
                 float *asum = reinterpret_cast<float *>(sm + Y.ag);   // [k*16 chunks][3]
-                if (tid < 32 * k) {
-                    bool got = false;
-                    for (uint32_t it = 0; it < kMaxSpins; ++it) {
-                        if (ld_acquire_u32(&sy->uflag[tid]) == tag) { got = true; break; }
-                        if (globaltimer_ns() > deadline) break;
-                        __nanosleep(32);
-                    }
-                    if (!got) NMOE_GIVEUP(6);
-                }
-                __syncthreads();
-#pragma unroll 1
-                for (int i0 = 0; i0 < k * kInter / 4; i0 += kThreads) {
-                    const int i = i0 + tid;
-                    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (i < k * kInter / 4) {
-                        v = __ldcg(reinterpret_cast<const float4 *>(sy->act) + i);
-                        const int e = 4 * i;
-                        *reinterpret_cast<float4 *>(actf + (e >> 5) * kXP + (e & 31)) = v;
-                    }
-                    if (kHalf) {   // 32 consecutive float4 = 128 columns of one slot
-                        float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-#pragma unroll
-                        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-                        if (lane == 0 && i < k * kInter / 4) atomicMax(&S->amax_bits[(4 * i) / kInter], __float_as_uint(m));
-                    }
-                    float e2 = v.x + v.z, o2 = v.y + v.w;
-#pragma unroll
-                    for (int m = 1; m < 8; m <<= 1) {
-                        e2 += __shfl_xor_sync(0xffffffffu, e2, m);
-                        o2 += __shfl_xor_sync(0xffffffffu, o2, m);
-                    }
-                    if (i < k * kInter / 4 && (i & 7) == 0) {
-                        asum[3 * (i >> 3)] = e2;
-                        asum[3 * (i >> 3) + 1] = o2;
-                        asum[3 * (i >> 3) + 2] = e2 + o2;
-                    }
-                }
-                __syncthreads();
-                if (kHalf) {
-                    __half2 *ah = reinterpret_cast<__half2 *>(sm + Y.acth);   // [k][256]
-#pragma unroll 1
-                    for (int e = tid; e < k * 256; e += kThreads) {
-                        const int sl = e >> 8;
-                        ah[e] = pair_entry<kBits>(actf + sl * (kInter / 32) * kXP, e & 255,
-                                                  half_exp(__uint_as_float(S->amax_bits[sl])));
-                    }
-                    __syncthreads();
-                }
-                NMOE_PHASE(6);
-                float *dpart = reinterpret_cast<float *>(sm + Y.part);   // [band][slot][16 rows]
+                const int wps = max(1, kWarps / k);
+                const int s = warp / wps, part = warp % wps;
+                const int gn = wps * 32, gt = tid - s * gn;
+                auto gsync = [&]() { asm volatile("bar.sync %0, %1;" ::"r"(1 + s), "r"(gn) : "memory"); };
                 bool bands_ok = true;
-                for (int i = 0; i < nB; ++i) bands_ok &= mbar_wait_warp(&bars[kBarBand0 + i], 0, deadline);
-                if (!bands_ok && lane == 0) NMOE_GIVEUP(7);
-                if (tid == 0) NMOE_STAMP(14);
+                if (s < k) {
+                    if (gt < 32) {
+                        bool got = false;
+                        for (uint32_t it = 0; it < kMaxSpins; ++it) {
+                            if (ld_acquire_u32(&sy->uflag[32 * s + gt]) == tag) { got = true; break; }
+                            if (globaltimer_ns() > deadline) break;
+                            __nanosleep(32);
+                        }
+                        if (!got) NMOE_GIVEUP(6);
+                    }
+                    gsync();
+#pragma unroll 1
+                    for (int i = gt; i < kInter / 4; i += gn) {   // uniform within a warp
+                        const int ii = s * (kInter / 4) + i;
+                        const float4 v = __ldcg(reinterpret_cast<const float4 *>(sy->act) + ii);
+                        const int e = 4 * ii;
+                        *reinterpret_cast<float4 *>(actf + (e >> 5) * kXP + (e & 31)) = v;
+                        if (kHalf) {
+                            float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+                            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                            if (lane == 0) atomicMax(&S->amax_bits[s], __float_as_uint(m));
+                        }
+                        float e2 = v.x + v.z, o2 = v.y + v.w;
+#pragma unroll
+                        for (int m = 1; m < 8; m <<= 1) {
+                            e2 += __shfl_xor_sync(0xffffffffu, e2, m);
+                            o2 += __shfl_xor_sync(0xffffffffu, o2, m);
+                        }
+                        if ((ii & 7) == 0) {
+                            asum[3 * (ii >> 3)] = e2;
+                            asum[3 * (ii >> 3) + 1] = o2;
+                            asum[3 * (ii >> 3) + 2] = e2 + o2;
+                        }
+                    }
+                    gsync();
+                    if (kHalf) {
+                        __half2 *ah = reinterpret_cast<__half2 *>(sm + Y.acth) + s * 256;
+                        const int E = half_exp(__uint_as_float(S->amax_bits[s]));
+#pragma unroll 1
+                        for (int e = gt; e < 256; e += gn) ah[e] = pair_entry<kBits>(actf + s * (kInter / 32) * kXP, e, E);
+                        gsync();
+                    }
+                    if (tid == 0) NMOE_STAMP(6);
+                    for (int i = 0; i < nB; ++i) bands_ok &= mbar_wait_warp(&bars[kBarBand0 + i], 0, deadline);
+                    if (!bands_ok && lane == 0) NMOE_GIVEUP(7);
+                    if (tid == 0) NMOE_STAMP(14);
+                }
+                float *dpart = reinterpret_cast<float *>(sm + Y.part);   // [band][slot][16 rows]
                 if (bands_ok) {
                     // warp -> (slot, part); lane -> (chunk of the 512 columns, row subgroup);
                     // the lane's act chunk stays in registers across its rows
                     constexpr int kLanesPer = kBits == 4 ? 16 : 8;   // chunks per down row
                     constexpr int kSubs = 32 / kLanesPer;
-                    const int wps = max(1, kWarps / k);
-                    const int s = warp / wps, part = warp % wps;
                     const int cc = lane % kLanesPer, sub = lane / kLanesPer;
                     const int stride = kSubs * wps;
                     const int npass = (16 + stride - 1) / stride;
