@@ -125,6 +125,26 @@ __device__ __forceinline__ bool poll_tagged4(const uint64_t *p, uint32_t tag, fl
         __nanosleep(64);
     }
 }
+// Poll 8 consecutive tagged words (64-byte aligned): all four loads of an attempt are in
+// flight together, so a successful attempt costs one L2 round trip.
+__device__ __forceinline__ bool poll_tagged8(const uint64_t *p, uint32_t tag, float *v, uint64_t deadline) {
+    for (uint32_t it = 0;; ++it) {
+        uint64_t a[8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            asm volatile("ld.volatile.global.v2.u64 {%0,%1}, [%2];" : "=l"(a[2 * j]), "=l"(a[2 * j + 1]) : "l"(p + 2 * j) : "memory");
+        bool all = true;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) all &= (uint32_t)(a[j] >> 32) == tag;
+        if (all) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = __uint_as_float((uint32_t)a[j]);
+            return true;
+        }
+        if (it >= kMaxSpins || globaltimer_ns() > deadline) return false;
+        __nanosleep(64);
+    }
+}
 __device__ __forceinline__ bool poll_tagged1(const uint64_t *p, uint32_t tag, float *v, uint64_t deadline) {
     for (uint32_t it = 0;; ++it) {
         uint64_t a;
@@ -589,12 +609,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
         // lane holds experts 8*lane .. 8*lane+7
         float v[8];
         bool ok = !S->abort;
-        // wait on one word per lane first (light polling), then read the lane's 8 words
-        float probe;
         const uint32_t want = P.stall ? tag + 1u : tag;
-        if (ok) ok = poll_tagged1(&sy->logits[8 * lane + 7], want, &probe, deadline) &&
-                     poll_tagged4(&sy->logits[8 * lane], want, v, deadline) &&
-                     poll_tagged4(&sy->logits[8 * lane + 4], want, v + 4, deadline);
+        if (ok) ok = poll_tagged8(&sy->logits[8 * lane], want, v, deadline);
         ok = __all_sync(0xffffffffu, ok);
         if (lane == 0) NMOE_STAMP(15);
         if (!ok) {
