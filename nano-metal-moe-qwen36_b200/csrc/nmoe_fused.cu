@@ -417,15 +417,22 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
     uint32_t tag;
     asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(tag) : "l"(&sy->epoch) : "memory");
     tag += 1u;
+    // x: each thread loads its 4 columns straight into registers (one L2 round trip)
+    uint4 xr4 = make_uint4(0u, 0u, 0u, 0u);
+    if (P.x_f32) {
+        xr4 = __ldcg(reinterpret_cast<const uint4 *>(P.x) + tid);
+    } else {
+        const uint2 u = __ldcg(reinterpret_cast<const uint2 *>(P.x) + tid);
+        xr4.x = u.x;
+        xr4.y = u.y;
+    }
     // residual rows this thread combines at the end: load early, latency hidden
     float hm_reg = 0.f;
     if (!P.route_only && P.h_mid && tid < nB * 16)   // volatile: keep the load here, not at its use
         asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(hm_reg) : "l"(P.h_mid + (band0 + (tid >> 4) * G) * 16 + (tid & 15)));
     if (tid == 0) {
         if (P.timeline) sy->tl[c & 1023][0] = (uint32_t)t_start;
-        const uint32_t xbytes = P.x_f32 ? kHidden * 4 : kHidden * 2;
-        mbar_arrive_expect_tx(&bars[kBarX], xbytes);
-        bulk_g2s(sm + Y.xraw, P.x, xbytes, &bars[kBarX], policy_evict_first());
+        mbar_arrive_expect_tx(&bars[kBarX], 0u);   // unused: x is loaded by the threads
     }
     // The shared-expert copies go out only once the router rows have landed (see phase
     // 2), so that the router bytes do not queue behind them in this SM's copy engine.
@@ -455,18 +462,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
     };
 
     // ---- 1. x: fp32 padded + per-32-column parity sums + per-64-column group sums -----
-    if (!mbar_wait_warp(&bars[kBarX], 0, deadline)) {
-        if (lane == 0) NMOE_GIVEUP(1);
-    }
     {
         const int col0 = 4 * tid;   // 512 threads x 4 columns
         float v[4];
         if (P.x_f32) {
-            const float4 f = *reinterpret_cast<const float4 *>(sm + Y.xraw + 16 * tid);
-            v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+            v[0] = __uint_as_float(xr4.x); v[1] = __uint_as_float(xr4.y);
+            v[2] = __uint_as_float(xr4.z); v[3] = __uint_as_float(xr4.w);
         } else {
-            const uint2 u = *reinterpret_cast<const uint2 *>(sm + Y.xraw + 8 * tid);
-            v[0] = bf16_lo(u.x); v[1] = bf16_hi(u.x); v[2] = bf16_lo(u.y); v[3] = bf16_hi(u.y);
+            v[0] = bf16_lo(xr4.x); v[1] = bf16_hi(xr4.x); v[2] = bf16_lo(xr4.y); v[3] = bf16_hi(xr4.y);
         }
         *reinterpret_cast<float4 *>(xs + (col0 >> 5) * kXP + (col0 & 31)) = make_float4(v[0], v[1], v[2], v[3]);
         float e = v[0] + v[2], o = v[1] + v[3];
