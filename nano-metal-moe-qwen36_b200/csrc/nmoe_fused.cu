@@ -755,7 +755,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
             {
                 float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
                 if (tid < 128 && !poll_tagged4(&sy->shared_act[4 * tid], tag, &v.x, deadline)) NMOE_GIVEUP(5);
-                if (tid == 0 && !poll_tagged1(&sy->score, tag, &S->score, deadline)) NMOE_GIVEUP(5);
+                if (tid == 128 && !poll_tagged1(&sy->score, tag, &S->score, deadline)) NMOE_GIVEUP(5);
                 __syncthreads();
                 if (tid < 128 && !S->abort) {
                     const int col = 4 * tid;
