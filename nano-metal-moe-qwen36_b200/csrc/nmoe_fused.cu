@@ -624,29 +624,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
                 reinterpret_cast<float4 *>(P.logits_out)[2 * lane + 1] = make_float4(v[4], v[5], v[6], v[7]);
             }
             const TopkLane tk = warp_topk_lane(v, k, lane);
-            // renormalised weight of selection s (lane s): exp(l_s - l_0) / sum_t exp(l_t - l_0),
-            // the sum taken in selection order
-            const float ex = lane < k ? expf(tk.val - tk.l0) : 0.f;
-            float sum = 0.f;
-#pragma unroll 1
-            for (int t = 0; t < k; ++t) sum += __shfl_sync(0xffffffffu, ex, t);
+            const uint32_t e = lane < k ? tk.idx : 0u;
+            const int valid = lane < k && e < (uint32_t)P.num_experts;
             if (lane < kMaxK) {
-                const int s = lane;
-                const uint32_t e = s < k ? tk.idx : 0u;
-                S->idx[s] = e;
-                const float w = s < k ? ex / sum : 0.f;
-                const int valid = s < k && e < (uint32_t)P.num_experts;
-                if (s < k && !valid) set_err(P.err, kErrExpertRange);
-                S->valid[s] = valid;
-                S->w[s] = valid ? w : 0.f;
-                if (c == 0) {
-                    if (P.idx_out) P.idx_out[s] = e;
-                    if (P.w_out) P.w_out[s] = w;
-                }
+                S->idx[lane] = e;
+                S->valid[lane] = valid;
             }
             __syncwarp();
-            // routed copies: gate/up units, then this CTA's output bands of every slot
-            if (lane == 0) NMOE_STAMP(9);
+            // routed copies first (gate/up units, then the band expectations); the weights
+            // are only needed at the combine
             if (lane == 0 && !P.route_only) {
                 const uint64_t pol = policy_evict_first();
                 for (int i = 0; i < nU; ++i) {
@@ -665,6 +651,22 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
                 if (nU == 0) issue_bands();
                 NMOE_STAMP(10);
             }
+            // renormalised weight of selection s (lane s): exp(l_s - l_0) / sum_t exp(l_t - l_0),
+            // the sum taken in selection order
+            const float ex = lane < k ? expf(tk.val - tk.l0) : 0.f;
+            float sum = 0.f;
+#pragma unroll 1
+            for (int t = 0; t < k; ++t) sum += __shfl_sync(0xffffffffu, ex, t);
+            if (lane < kMaxK) {
+                const float w = lane < k ? ex / sum : 0.f;
+                if (lane < k && !valid) set_err(P.err, kErrExpertRange);
+                S->w[lane] = valid ? w : 0.f;
+                if (c == 0) {
+                    if (P.idx_out) P.idx_out[lane] = e;
+                    if (P.w_out) P.w_out[lane] = w;
+                }
+            }
+            if (lane == 0) NMOE_STAMP(9);
         }
     }
     __syncthreads();
