@@ -150,6 +150,22 @@ def test_batched_matches_decode_routing():
     assert rel_l2(o[0], out1.cpu().numpy()) < OUT_TOL
 
 
+def test_batched_all_logits_tied():
+    """Identical router rows: every token's logits tie, and each token selects experts
+    0..k-1 with equal weights."""
+    ctx = N.Context(quant_bits=4, num_layers=1, t_max=64, device=0)
+    lw = O.make_layer(10, bits=4, distinct_experts=8)
+    r = lw.router["weight"].copy()
+    r[:] = r[9]
+    lw.router = {"dtype": N.DTYPE_BF16, "weight": r}
+    upload(ctx, 0, lw)
+    x, xd = make_x(4, 40, N.DTYPE_BF16)
+    o, idx, w, lg = run(ctx, 40, 8, xd, N.DTYPE_BF16)
+    assert (lg == lg[:, :1]).all()
+    np.testing.assert_array_equal(idx, np.tile(np.arange(8, dtype=np.uint32), (40, 1)))
+    np.testing.assert_allclose(w, 1.0 / 8, rtol=1e-6)
+
+
 def test_batched_argument_errors():
     ctx, lw = setup("cfg2_q4_bf16")
     x, xd = make_x(1, 4, N.DTYPE_BF16)

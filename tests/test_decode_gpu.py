@@ -126,6 +126,25 @@ def test_tie_goes_to_lower_expert_id():
         np.testing.assert_array_equal(idx[:k], ridx)
 
 
+def test_all_logits_tied_picks_lowest_ids():
+    """All 256 router rows identical: every logit ties, so the selection is experts
+    0..k-1 (lower id first) with equal weights."""
+    ctx = N.Context(quant_bits=4, num_layers=1, device=0)
+    lw = O.make_layer(9, bits=4, distinct_experts=8)
+    r = lw.router["weight"].copy()
+    r[:] = r[5]
+    lw.router = {"dtype": N.DTYPE_BF16, "weight": r}
+    upload(ctx, 0, lw)
+    x, xd = make_x(3, N.DTYPE_BF16)
+    for k in (1, 3, 8):
+        out, idx, w, lg = run_gpu(ctx, 0, k, xd, N.DTYPE_BF16)
+        assert (lg == lg[0]).all()
+        assert list(idx[:k]) == list(range(k))
+        np.testing.assert_allclose(w[:k], 1.0 / k, rtol=1e-6)
+        ridx, _ = O.route_reference(lg, k)
+        np.testing.assert_array_equal(idx[:k], ridx)
+
+
 def test_argument_errors():
     ctx, _ = setup("cfg0_q4_bf16")
     x, xd = make_x(1, N.DTYPE_BF16)
