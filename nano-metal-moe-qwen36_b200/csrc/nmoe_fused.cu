@@ -66,7 +66,7 @@ struct FusedSync {
 struct FusedLayout {
     uint32_t bars, ctl, xs, xsum, rw, sp, gv, sdn, units, bands, part, dsp, sred, total;
     // aliases inside `units` (dead once the routed gate/up is done)
-    uint32_t xraw, sact, ssum, actf, ag, acth;
+    uint32_t sact, ssum, actf, ag, acth;
     uint32_t xh;
     int nUmax, nBmax, nR, nS, kmax;
 };
@@ -981,8 +981,8 @@ static FusedLayout make_layout(int bits, bool rq4, bool sq4, int G, int kmax) {
     Y.dsp = take((Y.nR * 8 + Y.nS * 16 + 8) * 4);
     Y.sred = take(Y.nBmax * 16 * 4);
     Y.xh = take(1024 * 4);
-    // `units` last; the x staging buffer and the act buffers alias it (x is consumed
-    // before any routed copy is issued; act is staged after the routed gate/up is done)
+    // `units` last; the act buffers alias it (act is staged after the routed gate/up
+    // is done)
     Y.units = take(0);
     uint32_t ua = 0;
     auto utake = [&](uint32_t bytes) {
@@ -990,13 +990,12 @@ static FusedLayout make_layout(int bits, bool rq4, bool sq4, int G, int kmax) {
         ua += (bytes + 127) & ~127u;
         return o;
     };
-    Y.xraw = Y.units;
     Y.sact = utake((kInter / 32) * kXP * 4);
     Y.ssum = utake((kInter / 32) * 3 * 4);
     Y.actf = utake(kmax * (kInter / 32) * kXP * 4);
     Y.ag = utake(kmax * (kInter / 32) * 3 * 4);
     Y.acth = utake(kmax * 256 * 4);
-    const uint32_t unit_bytes = std::max(Y.nUmax * pg.bp, std::max(ua, (uint32_t)kHidden * 4));
+    const uint32_t unit_bytes = std::max(Y.nUmax * pg.bp, ua);
     Y.total = Y.units + unit_bytes;
     return Y;
 }
