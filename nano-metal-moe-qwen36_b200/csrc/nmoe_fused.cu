@@ -9,12 +9,11 @@
 //                                                    -> act
 //   output bands     b with (G-1-b) mod G == c       (16 output rows: k expert down
 //                                                    bands + shared down + combine)
-// All weight bytes move by cp.async.bulk straight into shared memory, each slice in one
+// Weight bytes move by cp.async.bulk straight into shared memory, each slice in one
 // copy thanks to the repacked HBM layout (nmoe_pack.cuh): the routing-independent ones
 // at kernel start, the routed ones as soon as this CTA knows the top-k. Routed gate/up
-// and down products run on the tensor cores (mma.sync m16n8k16 bf16): packed values
-// become exact bf16 integers in registers (LOP3 + SUB), the activation vector enters as
-// hi/lo bf16 columns (so fp32 inputs keep ~16 mantissa bits), and the affine
+// and down dots use the packed values in place as exact subnormal halves against a
+// per-call scaled half2 table of x (or act), flushed to fp32 once per word; the affine
 // dequantisation is applied per 64-column group as  s * sum(q*x) + b * sum(x).
 // Router and shared-expert rows (bf16 or q4) use an fp32 FFMA path.
 // Cross-CTA results (logits, shared act, score, act) are published as 64-bit words
