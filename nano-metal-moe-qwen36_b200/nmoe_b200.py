@@ -160,6 +160,45 @@ def _np_ptr(a) -> int | None:
     return None if a is None else a.ctypes.data
 
 
+# Stamp slots of the batch-1 kernel's timeline (k_moe_decode_fused, NMOE_TIMELINE=1).
+TIMELINE_SLOTS = {
+    1: "x staged",
+    8: "logits published",
+    2: "router units done",
+    15: "logits seen",
+    10: "routed copies issued",
+    9: "top-k weights done",
+    3: "routing barrier",
+    11: "first unit landed",
+    4: "act published",
+    12: "shared down done",
+    6: "act staged",
+    14: "down bands landed",
+    5: "down dots done",
+    7: "end",
+}
+
+
+def summarize_timeline(tl):
+    """Decode a [CTA][16] table of %globaltimer low words (slot 0 = CTA start, 0 = not
+    reached) into {phase name: (min, median, max)} microseconds after the earliest start."""
+    t = np.asarray(tl, np.int64)
+    ref = t[:, 0][t[:, 0] > 0][0]
+
+    def rel(v):   # signed difference of 32-bit stamp words (they wrap every ~4.3 s)
+        d = (v - ref) & 0xFFFFFFFF
+        return np.where(d >= 2**31, d - 2**32, d)
+
+    t0 = rel(t[:, 0][t[:, 0] > 0]).min()
+    out = {}
+    for slot, name in TIMELINE_SLOTS.items():
+        v = t[:, slot]
+        v = rel(v[v > 0]) - t0
+        if v.size:
+            out[name] = (v.min() / 1e3, float(np.median(v)) / 1e3, v.max() / 1e3)
+    return out
+
+
 class Context:
     """One nmoe_moe_ctx on one CUDA device."""
 
@@ -250,6 +289,12 @@ class Context:
         out = np.zeros((n_ctas, 16), np.uint32)
         self._check(self._L.nmoe_moe_debug_timeline(self.h, out.ctypes.data, n_ctas))
         return out
+
+    def timeline_phases(self, n_ctas=148):
+        """Per-phase times of the last batch-1 launch, in microseconds after the earliest
+        CTA start: {phase name: (min, median, max) over the CTAs that reached it}.
+        Needs a context created with NMOE_TIMELINE=1 in the environment."""
+        return summarize_timeline(self.debug_timeline(n_ctas))
 
     def device_status(self):
         code = C.c_int(0)

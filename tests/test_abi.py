@@ -5,6 +5,7 @@ import json
 import os
 import re
 
+import numpy as np
 import pytest
 
 import nmoe_b200 as N
@@ -94,3 +95,18 @@ def test_strerror():
     L = N.lib()
     assert L.nmoe_moe_strerror(N.OK) == b"ok"
     assert b"timed out" in L.nmoe_moe_strerror(N.ETIMEOUT)
+
+
+def test_timeline_summary_decodes_stamps():
+    """summarize_timeline: microseconds after the earliest CTA start, per named phase,
+    ignoring unreached slots and surviving a wrap of the 32-bit stamp words."""
+    base = 2**32 - 150    # the low word wraps between the CTAs' starts
+    tl = np.zeros((3, 16), np.uint32)
+    for c in range(3):
+        tl[c, 0] = (base + 100 * (2 - c)) & 0xFFFFFFFF
+        tl[c, 7] = (base + 20000 + 1000 * c) & 0xFFFFFFFF   # earliest start is CTA 2
+    tl[1, 11] = (base + 9000) & 0xFFFFFFFF
+    s = N.summarize_timeline(tl)
+    assert s["end"] == (20.0, 21.0, 22.0)
+    assert s["first unit landed"] == (9.0, 9.0, 9.0)
+    assert "act staged" not in s
