@@ -185,13 +185,18 @@ int nmoe_moe_nccl_unique_id(void *out, size_t bytes);
 int nmoe_moe_device_status(nmoe_moe_ctx *ctx, int *code);
 
 /* Diagnostics: copy and clear the single-launch decode kernel's per-CTA progress trail
- * (n <= 1024 entries; entry c = highest phase 1..7 CTA c reached since the last read,
- * 100 + phase where a bounded wait gave up). Synchronises the device. */
+ * (n <= 1024 entries; entry c = 100 + phase where a bounded wait of CTA c gave up; with
+ * NMOE_TIMELINE=1 at context creation also the highest phase 1..7 reached since the last
+ * read). Synchronises the device. No reference counterpart. */
 int nmoe_moe_debug_trail(nmoe_moe_ctx *ctx, uint32_t *out, int n);
-/* Diagnostics: per-CTA phase timestamps (globaltimer ns, low 32 bits, [n_ctas][16]) of
+/* Diagnostics: per-CTA phase timestamps (globaltimer ns, low 32 bits, [n_ctas][32]) of
  * the last decode call, recorded when the context was created with NMOE_TIMELINE=1 in
- * the environment. Synchronises the device. */
+ * the environment (slots a CTA did not reach in that call read 0). Synchronises the
+ * device. No reference counterpart. */
 int nmoe_moe_debug_timeline(nmoe_moe_ctx *ctx, uint32_t *out, int n_ctas);
+/* Diagnostics: CTAs of the batch-1 decode kernel's grid (one per SM, at most 256), i.e.
+ * the rows nmoe_moe_debug_timeline fills. No reference counterpart. */
+int nmoe_moe_decode_grid(const nmoe_moe_ctx *ctx);
 
 /* Diagnostics: copy the router logits [T][256] (fp32) of the last
  * nmoe_moe_forward_batched call to host memory (T <= that call's T). Synchronises the

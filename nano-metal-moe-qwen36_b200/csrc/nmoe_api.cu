@@ -322,6 +322,29 @@ extern "C" int nmoe_moe_set_dense(nmoe_moe_ctx *ctx, int layer, const nmoe_moe_d
     }
     put_row(&h[A.gvec], src[4], sq4, 0, NMOE_HIDDEN);
     for (int r = 0; r < NMOE_HIDDEN; ++r) put_row(&h[A.sdown + (size_t)r * A.sdrow], src[3], sq4, r, NMOE_INTER);
+    // the shared down again by columns for the batch-1 kernel (nmoe_pack.cuh, sdown_t)
+    if (!sq4) {
+        const uint16_t *dw = static_cast<const uint16_t *>(src[3]->weight);
+        uint16_t *t = reinterpret_cast<uint16_t *>(&h[A.sdown_t]);
+        for (int r = 0; r < NMOE_HIDDEN; ++r)
+            for (int c = 0; c < NMOE_INTER; ++c) t[(size_t)c * NMOE_HIDDEN + r] = dw[(size_t)r * NMOE_INTER + c];
+    } else {
+        const uint32_t *dw = static_cast<const uint32_t *>(src[3]->weight);   // [2048][64] words
+        uint32_t *t = reinterpret_cast<uint32_t *>(&h[A.sdown_t]);             // [512][256] words
+        for (int r = 0; r < NMOE_HIDDEN; ++r)
+            for (int c = 0; c < NMOE_INTER; ++c) {
+                const uint32_t q = (dw[(size_t)r * 64 + c / 8] >> (4 * (c % 8))) & 0xFu;
+                t[(size_t)c * 256 + r / 8] |= q << (4 * (r % 8));
+            }
+        const uint16_t *ss = static_cast<const uint16_t *>(src[3]->scales);
+        const uint16_t *sb = static_cast<const uint16_t *>(src[3]->biases);
+        uint16_t *ts = reinterpret_cast<uint16_t *>(&h[A.sdown_t + 512 * 1024]);
+        for (int g = 0; g < 8; ++g)
+            for (int r = 0; r < NMOE_HIDDEN; ++r) {
+                ts[g * NMOE_HIDDEN + r] = ss[r * 8 + g];
+                ts[8 * NMOE_HIDDEN + g * NMOE_HIDDEN + r] = sb[r * 8 + g];
+            }
+    }
     DeviceGuard guard(ctx->device);
     NMOE_CUDA_TRY(ctx, cudaMemcpy(ctx->d_dense + (size_t)layer * ctx->dense_layer_bytes, h.data(), A.total,
                                   cudaMemcpyHostToDevice));
@@ -361,7 +384,7 @@ static FusedCall make_call(nmoe_moe_ctx *ctx, int layer, int k, const void *x, i
     a.router = d + A.router;
     a.spairs = d + A.spairs;
     a.gvec = d + A.gvec;
-    a.sdown = d + A.sdown;
+    a.sdown_t = d + A.sdown_t;
     a.x = x;
     a.x_f32 = x_dtype == NMOE_DTYPE_F32;
     a.h_mid = h_mid;

@@ -401,6 +401,35 @@ bool make_matrix_maps(BatchedState *B, GemmProblem &pr, int m, const uint8_t *ba
            make_map(B, &pr.tb[m], base + b_off, false, ng, s_row_stride, bands, band_stride, groups, group_stride, 8);
 }
 
+// Column-major maps of the routed down matrices (down group slabs, nmoe_pack.cuh):
+// weights (2048 rows, wpg word columns, 8 slabs, experts), box 128 rows x wpg words;
+// scales / biases (2048 rows, 1, 8 slabs, experts), box 128 rows x 8 slabs.
+bool make_cm_maps(BatchedState *B, GemmProblem &pr, const uint8_t *down, const PackGeo &pg, int n_experts) {
+    pr.a_cm = 1;
+    {
+        const cuuint64_t dims[4] = {2048, pg.wpg, 8, (cuuint64_t)n_experts};
+        const cuuint64_t strides[3] = {2048 * 4, pg.dslab, pg.esz};
+        const cuuint32_t box[4] = {128, pg.wpg, 1, 1};
+        const cuuint32_t es[4] = {1, 1, 1, 1};
+        if (B->encode(&pr.tw[0], CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, const_cast<uint8_t *>(down), dims, strides, box, es,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return false;
+    }
+    for (int which = 0; which < 2; ++which) {
+        const cuuint64_t dims[4] = {2048, 1, 8, (cuuint64_t)n_experts};
+        const cuuint64_t strides[3] = {4096, pg.dslab, pg.esz};
+        const cuuint32_t box[4] = {128, 1, 8, 1};
+        const cuuint32_t es[4] = {1, 1, 1, 1};
+        CUtensorMap *m = which ? &pr.tb[0] : &pr.ts[0];
+        if (B->encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, const_cast<uint8_t *>(down + pg.dslab_w + which * 4096),
+                      dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return false;
+    }
+    return true;
+}
+
 // The kernel instantiation for the problems of a launch (see k_moe_gemm's parameters).
 using GemmKernel = void (*)(const GemmParams);
 #define NMOE_GEMM_KINDS(X)                                                      \
@@ -827,8 +856,7 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
         r.epi = kEpiBf16;
         r.ld_out = kHidden;
         r.out = E ? E->yr : B->y;
-        bool ok = make_matrix_maps(B, r, 0, experts + pg.gu_bytes, bits, kInter, pg.wd * 4, 128, pg.db, ctx->n_local,
-                                   pg.esz, pg.tile_band_d, pg.tile_band_d + 256, 16);
+        bool ok = make_cm_maps(B, r, experts + pg.gu_bytes, pg, ctx->n_local);
         GemmProblem &s = P.prob[1];
         s.fmt = sfmt;
         s.n_mat = 1;

@@ -6,7 +6,7 @@
 namespace nmoe {
 struct FusedCall {
     const uint8_t *experts;                          // repacked blobs of this layer (this rank's)
-    const uint8_t *router, *spairs, *gvec, *sdown;   // repacked dense regions of this layer
+    const uint8_t *router, *spairs, *gvec, *sdown_t;   // repacked dense regions of this layer
     const uint8_t *next_dense;                       // next layer's dense arena (L2 prefetch) or null
     uint32_t next_dense_bytes;
     const void *x;

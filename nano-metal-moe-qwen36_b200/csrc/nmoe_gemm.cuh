@@ -65,6 +65,8 @@ struct alignas(64) GemmProblem {
     CUtensorMap tb[2];        // biases
     CUtensorMap tx[2];        // B rows (2D: K columns, rows; box 64 x 16, 128B swizzle): hi, lo
     int fmt;                  // kAFmt*
+    int a_cm;                 // weights in down group slabs: tiles [wpg words][128 rows]
+                              // (column-major), scales/biases [8 groups][128 rows]
     int n_mat;                // 2 = gate+up, 1 otherwise
     int K;                    // 2048 or 512
     int m_tiles;              // rows / 128
@@ -352,16 +354,33 @@ __device__ __forceinline__ void dq_load(const uint8_t *raw, int h, uint32_t *gw)
     }
 }
 
+// Same groups from a column-major tile ([word column][128 rows] u32, row r).
+template <int kFmt>
+__device__ __forceinline__ void dq_load_cm(const uint8_t *raw, int r, int h, uint32_t *gw) {
+    const uint32_t *w = reinterpret_cast<const uint32_t *>(raw) + r;
+    if (kFmt == kAFmtQ4) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) gw[i] = w[(4 * h + i) * 128];
+    } else {
+        const uint32_t a = w[(2 * h) * 128], b = w[(2 * h + 1) * 128];
+        const uint32_t g0 = a & 0xFFFFu, g1 = a >> 16, g2 = b & 0xFFFFu, g3 = b >> 16;
+        gw[0] = g0 | (g0 << 8); gw[1] = g1 | (g1 << 8);
+        gw[2] = g2 | (g2 << 8); gw[3] = g3 | (g3 << 8);
+    }
+}
+
 // taddr: this thread's lane, column of matrix 0's half h; matrix m at +32 m.
-template <int kFmt, int kNMat>
+// kCM: single-matrix column-major tile (raw = the slot, cm_r = the row).
+template <int kFmt, int kNMat, bool kCM = false>
 __device__ __forceinline__ void dq_step_q(const uint8_t *raw, int rawm, const uint8_t *sc, int sidx, uint32_t taddr,
-                                          int h) {
+                                          int h, int cm_r = 0) {
     constexpr int sh = kFmt == kAFmtQ4 ? 4 : 2;
     constexpr uint32_t mask = kFmt == kAFmtQ4 ? 0x000F000Fu : 0x00030003u;
     uint32_t gw[kNMat][4], s2[kNMat], b2[kNMat];
 #pragma unroll
     for (int m = 0; m < kNMat; ++m) {
-        dq_load<kFmt>(raw + m * rawm, h, gw[m]);
+        if (kCM) dq_load_cm<kFmt>(raw, cm_r, h, gw[m]);
+        else dq_load<kFmt>(raw + m * rawm, h, gw[m]);
         const uint32_t s16 = reinterpret_cast<const uint16_t *>(sc + m * kGemmScStage)[sidx];
         const uint32_t b16 = reinterpret_cast<const uint16_t *>(sc + m * kGemmScStage + 2048)[sidx];
         s2[m] = s16 | (s16 << 16);
@@ -505,7 +524,7 @@ __device__ __forceinline__ bool dq_wait_a_free(const DqCtx &D) {
 }
 
 // One pass over the steps [ks0, ks0 + kb) of an item, q4/q2 weights.
-template <int kFmt, int kNMat, bool kSplit>
+template <int kFmt, int kNMat, bool kSplit, bool kCM = false>
 __device__ bool dq_run_q(DqCtx &D, const StepGeo &G, int ks0, bool lo) {
     GemmSmem *S = D.S;
     const int lane = threadIdx.x & 31;
@@ -528,14 +547,14 @@ __device__ bool dq_run_q(DqCtx &D, const StepGeo &G, int ks0, bool lo) {
         if (!__all_sync(0xffffffffu, mbar_wait_sleep(&S->raw_full[D.raw.idx], D.raw.phase, D.deadline))) return false;
         if (S->abort) return false;
         dq_trace(D, 2, D.a.count);
-        const uint8_t *src = D.sRaw + D.raw.idx * kGemmSlot + D.r * G.rowb;
+        const uint8_t *src = D.sRaw + D.raw.idx * kGemmSlot + (kCM ? 0 : D.r * G.rowb);
         const uint8_t *scp = D.sSc + si * 2 * kGemmScStage;
-        const int sidx = D.r * 8 + (ks & 7);
+        const int sidx = kCM ? (ks & 7) * 128 + D.r : D.r * 8 + (ks & 7);
         const uint32_t ta = D.tlane + D.a.idx * kGemmACols;
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
             if (kSplit) dq_step_split<kFmt>(src, scp, sidx, ta + 16 * hh, hh, lo);
-            else dq_step_q<kFmt, kNMat>(src, G.rawm, scp, sidx, ta + 16 * hh, hh);
+            else dq_step_q<kFmt, kNMat, kCM>(src, G.rawm, scp, sidx, ta + 16 * hh, hh, D.r);
         }
         tc_wait_st();
         tc_fence_before();
@@ -595,10 +614,12 @@ __device__ bool dq_run_bf16(DqCtx &D, const StepGeo &G, int ks0, bool zero) {
 
 // One dequant pass of a problem whose (format, matrices, split) are compile-time: each
 // kernel instantiation carries only the conversion code its problems use.
-template <int kFmt, int kNMat, int kSplit>
+// Problem 0 of a single-matrix q-format non-split launch is the routed down product,
+// whose weights are the column-major group slabs (kCM).
+template <int kFmt, int kNMat, int kSplit, bool kCM = false>
 __device__ __forceinline__ bool dq_pass(DqCtx &D, const StepGeo &G, int ks0, bool lo) {
     if constexpr (kFmt == kAFmtBf16) return dq_run_bf16<kNMat>(D, G, ks0, kSplit && lo);
-    else return dq_run_q<kFmt, kNMat, kSplit != 0>(D, G, ks0, lo);
+    else return dq_run_q<kFmt, kNMat, kSplit != 0, kCM && kNMat == 1 && kSplit == 0>(D, G, ks0, lo);
 }
 
 // Template parameters: (format, matrices, split) of problem 0 and of problem 1.
@@ -670,17 +691,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
                                 mbar_arrive_expect_tx(&S->sc_full[si], pr.n_mat * kGemmScStage);
                                 for (int m = 0; m < pr.n_mat; ++m) {
                                     uint8_t *d = sSc + (si * 2 + m) * kGemmScStage;
-                                    tma_load_4d(d, &pr.ts[m], ks & ~7, 0, w.mt * 8, w.e, &S->sc_full[si]);
-                                    tma_load_4d(d + 2048, &pr.tb[m], ks & ~7, 0, w.mt * 8, w.e, &S->sc_full[si]);
+                                    if (pr.a_cm) {
+                                        tma_load_4d(d, &pr.ts[m], w.mt * 128, 0, ks & ~7, w.e, &S->sc_full[si]);
+                                        tma_load_4d(d + 2048, &pr.tb[m], w.mt * 128, 0, ks & ~7, w.e, &S->sc_full[si]);
+                                    } else {
+                                        tma_load_4d(d, &pr.ts[m], ks & ~7, 0, w.mt * 8, w.e, &S->sc_full[si]);
+                                        tma_load_4d(d + 2048, &pr.tb[m], ks & ~7, 0, w.mt * 8, w.e, &S->sc_full[si]);
+                                    }
                                 }
                                 sc.next();
                             }
                             if (!mbar_wait_sleep(&S->raw_empty[raw.idx], raw.phase ^ 1, deadline)) { ok = false; break; }
                             trace_put(P, 0, raw.count);
                             mbar_arrive_expect_tx(&S->raw_full[raw.idx], pr.n_mat * G.rawm);
-                            for (int m = 0; m < pr.n_mat; ++m)
-                                tma_load_4d(sRaw + raw.idx * kGemmSlot + m * G.rawm, &pr.tw[m], ks * G.wpk, 0, w.mt * 8,
-                                            w.e, &S->raw_full[raw.idx]);
+                            for (int m = 0; m < pr.n_mat; ++m) {
+                                if (pr.a_cm)
+                                    tma_load_4d(sRaw + raw.idx * kGemmSlot, &pr.tw[m], w.mt * 128, 0, ks, w.e,
+                                                &S->raw_full[raw.idx]);
+                                else
+                                    tma_load_4d(sRaw + raw.idx * kGemmSlot + m * G.rawm, &pr.tw[m], ks * G.wpk, 0,
+                                                w.mt * 8, w.e, &S->raw_full[raw.idx]);
+                            }
                             raw.next();
                         } else {
                             const int bands = 8 / G.nslot;
@@ -812,7 +843,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
             const int npass = __popc(pr.passes), ks0 = w.sp * G.kb;
             for (int ps = 0; ps < npass && ok; ++ps) {
                 const bool lo = gemm_pass(pr.passes, ps) == 2;
-                ok = w.p == 0 ? dq_pass<F0, M0, S0>(D, G, ks0, lo) : dq_pass<F1, M1, S1>(D, G, ks0, lo);
+                ok = w.p == 0 ? dq_pass<F0, M0, S0, true>(D, G, ks0, lo) : dq_pass<F1, M1, S1>(D, G, ks0, lo);
             }
         }
         if (!ok && lane == 0) gemm_fail(S, P.err);

@@ -1,6 +1,6 @@
 // nmoe_repack.cu -- converter layout (EXPERT_LAYOUT, scripts/convert_qwen36.py:38-64)
-// -> the decode kernel's band layout (nmoe_pack.cuh). One thread per 32-bit word of the
-// destination; a pure permutation (same byte count).
+// -> the kernel layout of nmoe_pack.cuh (gate/up band pairs, down group slabs). One
+// thread per 32-bit word of the destination; a pure permutation (same byte count).
 #include "nmoe_fused.cuh"
 #include "nmoe_pack.cuh"
 
@@ -24,13 +24,18 @@ __global__ void k_repack(const uint8_t *__restrict__ src, uint8_t *__restrict__ 
                 const uint32_t comp[4] = {eo.gs, eo.gb, eo.us, eo.ub};
                 s = comp[which] + 16 * bp * 64 + q;
             }
-        } else {
-            const uint32_t d2 = d - pg.gu_bytes, b = d2 / pg.db, r = d2 % pg.db;
-            if (r < pg.tile_band_d) {
-                s = eo.dw + 16 * b * pg.wd * 4 + r;
-            } else {
-                const uint32_t r2 = r - pg.tile_band_d, which = r2 / 256, q = r2 % 256;
-                s = (which ? eo.db : eo.ds) + 16 * b * 16 + q;
+        } else {   // down group slab g: word columns [j][2048 rows], then s[2048], b[2048]
+            const uint32_t d2 = d - pg.gu_bytes, g = d2 / pg.dslab, r = d2 % pg.dslab;
+            if (r < pg.dslab_w) {
+                const uint32_t j = r / (2048 * 4), row = (r % (2048 * 4)) / 4;
+                s = eo.dw + (row * pg.wd + g * pg.wpg + j) * 4;
+            } else {   // two bf16 of consecutive rows: assembled from the [2048][8] tables
+                const uint32_t r2 = r - pg.dslab_w, which = r2 / 4096, row = (r2 % 4096) / 2;
+                const uint8_t *base = src + e * pg.esz + (which ? eo.db : eo.ds);
+                const uint32_t lo = *reinterpret_cast<const uint16_t *>(base + (row * 8 + g) * 2);
+                const uint32_t hi = *reinterpret_cast<const uint16_t *>(base + ((row + 1) * 8 + g) * 2);
+                reinterpret_cast<uint32_t *>(dst)[wi] = lo | (hi << 16);
+                continue;
             }
         }
         reinterpret_cast<uint32_t *>(dst)[wi] = *reinterpret_cast<const uint32_t *>(src + e * pg.esz + s);

@@ -13,9 +13,13 @@ struct TopkScratch {
 };
 
 // Order-preserving key of a float: unsigned comparison of keys is float comparison
-// (-0 and +0 map to one key, as they compare equal).
+// (-0 and +0 map to one key, as they compare equal). NaN maps to 1, below every other
+// key (-inf is 0x007FFFFF) and above the popped-head sentinel 0: the reference's strict
+// `>` never prefers a NaN (src/math.m:112-117), so a NaN logit is taken only once no
+// other logit is left, lowest expert id first.
 __device__ __forceinline__ uint32_t topk_key(float f) {
     const uint32_t u = __float_as_uint(f + 0.0f);
+    if (f != f) return 1u;
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 __device__ __forceinline__ float topk_val(uint32_t key) {
@@ -72,6 +76,53 @@ __device__ __forceinline__ TopkLane warp_topk_lane(const float *v, int k, int la
         key[7] = me ? 0u : key[7];
     }
     return out;
+}
+
+// The same selection with a shorter chain per round: the winning lane writes its id to
+// sidx[r] and every lane writes sval[r] = the round's maximum (shared memory, read after
+// a __syncwarp), so a round is one warp max, one ballot and the pop; the winner is the
+// lowest lane holding the maximum (no lane index is moved between lanes). Returns the
+// largest logit (l0) on every lane.
+__device__ __forceinline__ float warp_topk_smem(const float *v, int k, int lane, uint32_t *sidx, float *sval) {
+    uint32_t key[8], id[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        key[j] = topk_key(v[j]);
+        id[j] = (uint32_t)(8 * lane + j);
+    }
+#pragma unroll
+    for (int ph = 0; ph < 8; ++ph)
+#pragma unroll
+        for (int j = ph & 1; j + 1 < 8; j += 2) {
+            const bool sw = key[j + 1] > key[j];
+            const uint32_t ka = key[j], kb = key[j + 1], ia = id[j], ib = id[j + 1];
+            key[j] = sw ? kb : ka;
+            key[j + 1] = sw ? ka : kb;
+            id[j] = sw ? ib : ia;
+            id[j + 1] = sw ? ia : ib;
+        }
+    uint32_t lt;
+    asm("mov.u32 %0, %%lanemask_lt;" : "=r"(lt));
+    float l0 = 0.f;
+#pragma unroll 1
+    for (int r = 0; r < k; ++r) {
+        const uint32_t m = __reduce_max_sync(0xffffffffu, key[0]);
+        const bool eq = key[0] == m;
+        const uint32_t bal = __ballot_sync(0xffffffffu, eq);
+        const bool me = eq && (bal & lt) == 0u;   // lowest lane holding the maximum
+        const float mv = topk_val(m);
+        if (me) sidx[r] = id[0];
+        if (lane == 0) sval[r] = mv;
+        if (r == 0) l0 = mv;
+#pragma unroll
+        for (int j = 0; j < 7; ++j) {   // pop the head; 0 is below every other key
+            key[j] = me ? key[j + 1] : key[j];
+            id[j] = me ? id[j + 1] : id[j];
+        }
+        key[7] = me ? 0u : key[7];
+    }
+    __syncwarp();
+    return l0;
 }
 
 // Same selection, written to S->idx[0..k) and S->sel_v[0..k).

@@ -29,7 +29,7 @@ ABI_SYMBOLS = (
     "nmoe_moe_load_layer", "nmoe_moe_load_layer_file", "nmoe_moe_set_dense",
     "nmoe_moe_forward", "nmoe_moe_route", "nmoe_moe_forward_batched", "nmoe_moe_device_status",
     "nmoe_moe_forward_static", "nmoe_moe_static_error", "nmoe_moe_debug_trail", "nmoe_moe_debug_timeline",
-    "nmoe_moe_debug_logits", "nmoe_moe_debug_gemm_trace", "nmoe_moe_nccl_unique_id",
+    "nmoe_moe_debug_logits", "nmoe_moe_debug_gemm_trace", "nmoe_moe_nccl_unique_id", "nmoe_moe_decode_grid",
 )
 
 
@@ -110,6 +110,8 @@ def lib() -> C.CDLL:
     L.nmoe_moe_debug_trail.argtypes = [vp, vp, i]
     L.nmoe_moe_debug_timeline.restype = i
     L.nmoe_moe_debug_timeline.argtypes = [vp, vp, i]
+    L.nmoe_moe_decode_grid.restype = i
+    L.nmoe_moe_decode_grid.argtypes = [vp]
     L.nmoe_moe_debug_logits.restype = i
     L.nmoe_moe_debug_logits.argtypes = [vp, vp, i]
     L.nmoe_moe_nccl_unique_id.restype = i
@@ -161,26 +163,32 @@ def _np_ptr(a) -> int | None:
 
 
 # Stamp slots of the batch-1 kernel's timeline (k_moe_decode_fused, NMOE_TIMELINE=1).
+TIMELINE_WIDTH = 32
 TIMELINE_SLOTS = {
+    16: "dependency wait done",
     1: "x staged",
+    18: "router rows ready (warp 0)",
+    19: "router dot done (warp 0)",
+    20: "last router unit done",
     8: "logits published",
-    2: "router units done",
+    2: "router and shared rows done",
+    13: "logits poll starts",
     15: "logits seen",
+    6: "top-k ids done",
+    17: "unit 0 copies issued",
     10: "routed copies issued",
     9: "top-k weights done",
     3: "routing barrier",
-    11: "first unit landed",
-    4: "act published",
     12: "shared down done",
-    6: "act staged",
-    14: "down bands landed",
-    5: "down dots done",
+    11: "first unit landed",
+    14: "unit 0 gate/up done",
+    5: "routed units done",
     7: "end",
 }
 
 
 def summarize_timeline(tl):
-    """Decode a [CTA][16] table of %globaltimer low words (slot 0 = CTA start, 0 = not
+    """Decode a [CTA][slots] table of %globaltimer low words (slot 0 = CTA start, 0 = not
     reached) into {phase name: (min, median, max)} microseconds after the earliest start."""
     t = np.asarray(tl, np.int64)
     ref = t[:, 0][t[:, 0] > 0][0]
@@ -192,6 +200,8 @@ def summarize_timeline(tl):
     t0 = rel(t[:, 0][t[:, 0] > 0]).min()
     out = {}
     for slot, name in TIMELINE_SLOTS.items():
+        if slot >= t.shape[1]:
+            continue
         v = t[:, slot]
         v = rel(v[v > 0]) - t0
         if v.size:
@@ -285,12 +295,17 @@ class Context:
         self._check(self._L.nmoe_moe_debug_trail(self.h, out.ctypes.data, n))
         return out
 
-    def debug_timeline(self, n_ctas=148):
-        out = np.zeros((n_ctas, 16), np.uint32)
+    def decode_grid(self) -> int:
+        """CTAs of the batch-1 decode kernel's grid (one per SM)."""
+        return int(self._L.nmoe_moe_decode_grid(self.h))
+
+    def debug_timeline(self, n_ctas=None):
+        n_ctas = self.decode_grid() if n_ctas is None else n_ctas
+        out = np.zeros((n_ctas, TIMELINE_WIDTH), np.uint32)
         self._check(self._L.nmoe_moe_debug_timeline(self.h, out.ctypes.data, n_ctas))
         return out
 
-    def timeline_phases(self, n_ctas=148):
+    def timeline_phases(self, n_ctas=None):
         """Per-phase times of the last batch-1 launch, in microseconds after the earliest
         CTA start: {phase name: (min, median, max) over the CTAs that reached it}.
         Needs a context created with NMOE_TIMELINE=1 in the environment."""
