@@ -217,19 +217,29 @@ int nmoe_moe_debug_gemm_trace(nmoe_moe_ctx *ctx, uint32_t *out, int n);
  * All weights are DEVICE pointers the caller owns, laid out as nmoe_moe_load_layer /
  * nmoe_moe_set_dense take them on the host: `experts` is a layer_XX.bin image of
  * num_experts expert blobs, `dense` holds the router/shared tensors. The call allocates
- * nothing: its scratch (about 22 KB) is one array compiled into the library, held by
- * every GPU that loads it until the process exits, and shared by all calls on a device.
+ * nothing: its scratch (19,712 bytes, nmoe_moe_static_scratch_bytes()) is one array
+ * compiled into the library, held by every GPU that loads it until the process exits,
+ * and shared by all calls on a device. It runs four fp32 kernels (router + shared
+ * expert, top-k, routed gate/up, down + combine).
  * Limits: k in [1, 8] (the scratch holds 8 routed slots); larger k is rejected with
  * NMOE_EINVAL. The first call on a device (the current one) looks up that array's device
  * address; make that first call before any stream capture. Calls that overlap on the
  * GPU (different streams, or different host threads) race on the shared scratch: order
- * them. Routed ids >= num_experts contribute nothing. Message of a failed call:
- * nmoe_moe_static_error(). */
+ * them. Routed ids >= num_experts contribute nothing and set the scratch's error word,
+ * which nmoe_moe_static_status reads. Message of a failed call: nmoe_moe_static_error(). */
 int nmoe_moe_forward_static(const void *experts, int num_experts, int quant_bits,
                             const nmoe_moe_dense_weights *dense, int router_dtype, int shared_dtype,
                             int k, const void *x, int x_dtype, const float *h_mid, float *out,
                             uint32_t *idx_out, float *w_out, void *stream);
 const char *nmoe_moe_static_error(void);
+/* No counterpart in the reference. Bytes of the static scratch array. */
+size_t nmoe_moe_static_scratch_bytes(void);
+/* No counterpart in the reference. Read and clear the error word that the last
+ * nmoe_moe_forward_static call on the current device left in the static scratch (each
+ * call clears it when it starts), waiting for `stream` first. Allocates nothing. Returns
+ * NMOE_OK, NMOE_EDEVICE (routed expert id >= num_experts) or NMOE_ETIMEOUT, with the code
+ * in *code (may be NULL). Races, like the calls, with static calls that overlap it. */
+int nmoe_moe_static_status(int *code, void *stream);
 
 #ifdef __cplusplus
 }

@@ -704,6 +704,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
                 rpart[u] = v;
                 __threadfence_block();
                 if (atomicAdd(&S->rdone, 1) == uR - 1) {
+                    __threadfence_block();   // the other warps' partials, read below
                     if (kTL) NMOE_STAMP(20);
                     for (int r = 0; r < nR; ++r) {
                         float t = 0.f;

@@ -45,6 +45,32 @@ int fail(int code, const char *msg) {
 
 extern "C" const char *nmoe_moe_static_error(void) { return g_static_error; }
 
+extern "C" size_t nmoe_moe_static_scratch_bytes(void) { return kStaticScratchBytes; }
+
+extern "C" int nmoe_moe_static_status(int *code, void *stream) {
+    g_static_error[0] = 0;
+    if (code) *code = 0;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return fail(NMOE_ECUDA, "no usable current CUDA device");
+    StaticScratch *scr;
+    {
+        std::lock_guard<std::mutex> lk(g_mu);
+        scr = g_scratch_ptr[dev];
+    }
+    if (scr == nullptr) return NMOE_OK;   // no call has run on this device
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int h = 0;   // the word is read into this stack variable: nothing is allocated
+    cudaError_t e = cudaMemcpyAsync(&h, scr->err, sizeof h, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(scr->err, 0, sizeof(int), st);
+    if (e != cudaSuccess) return fail(NMOE_ECUDA, cudaGetErrorString(e));
+    if (code) *code = h;
+    if (h == 0) return NMOE_OK;
+    snprintf(g_static_error, sizeof g_static_error, "device error word = %d (%s)", h,
+             h == kErrExpertRange ? "routed expert id out of range" : h == kErrTimeout ? "bounded wait expired" : "unknown");
+    return h == kErrTimeout ? NMOE_ETIMEOUT : NMOE_EDEVICE;
+}
+
 extern "C" int nmoe_moe_forward_static(const void *experts, int num_experts, int quant_bits,
                                        const nmoe_moe_dense_weights *dense, int router_dtype, int shared_dtype,
                                        int k, const void *x, int x_dtype, const float *h_mid, float *out,

@@ -30,6 +30,7 @@ ABI_SYMBOLS = (
     "nmoe_moe_forward", "nmoe_moe_route", "nmoe_moe_forward_batched", "nmoe_moe_device_status",
     "nmoe_moe_forward_static", "nmoe_moe_static_error", "nmoe_moe_debug_trail", "nmoe_moe_debug_timeline",
     "nmoe_moe_debug_logits", "nmoe_moe_debug_gemm_trace", "nmoe_moe_nccl_unique_id", "nmoe_moe_decode_grid",
+    "nmoe_moe_static_scratch_bytes", "nmoe_moe_static_status",
 )
 
 
@@ -106,6 +107,9 @@ def lib() -> C.CDLL:
     L.nmoe_moe_forward_static.restype = i
     L.nmoe_moe_forward_static.argtypes = [vp, i, i, C.POINTER(DenseWeights), i, i, i, vp, i, vp, vp, vp, vp, vp]
     L.nmoe_moe_static_error.restype = C.c_char_p
+    L.nmoe_moe_static_scratch_bytes.restype = sz
+    L.nmoe_moe_static_status.restype = i
+    L.nmoe_moe_static_status.argtypes = [C.POINTER(i), vp]
     L.nmoe_moe_debug_trail.restype = i
     L.nmoe_moe_debug_trail.argtypes = [vp, vp, i]
     L.nmoe_moe_debug_timeline.restype = i
@@ -331,3 +335,11 @@ def forward_static(experts, num_experts, quant_bits, dense, router_dtype, shared
                                    k, _ptr(x), x_dtype, _ptr(h_mid), _ptr(out), _ptr(idx_out), _ptr(w_out), stream)
     if rc != OK:
         raise NmoeError(rc, L.nmoe_moe_static_error().decode())
+
+
+def static_status(stream=0):
+    """nmoe_moe_static_status: (status, code) of the last static call on this device."""
+    L = lib()
+    code = C.c_int(0)
+    rc = L.nmoe_moe_static_status(C.byref(code), stream)
+    return rc, code.value

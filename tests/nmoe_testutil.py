@@ -18,3 +18,15 @@ def rel_l2(a, b):
 
 def bf16_round(x: np.ndarray) -> np.ndarray:
     return O.bf16_to_f32(O.f32_to_bf16(x))
+
+
+_distinct = {}
+
+
+def distinct_layer(bits: int = 4) -> "O.LayerWeights":
+    """One layer whose 256 expert slots all hold different packs (no e % n reuse), so a
+    kernel that reads the wrong slot cannot match the oracle by accident. ~20 s of host
+    work, built once per process."""
+    if bits not in _distinct:
+        _distinct[bits] = O.make_layer(9001 + bits, bits=bits, distinct_experts=None)
+    return _distinct[bits]

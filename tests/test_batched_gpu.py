@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 
 import nmoe_b200 as N
-from nmoe_testutil import rel_l2, upload
+from nmoe_testutil import distinct_layer, rel_l2, upload
 from oracle import oracle as O
 
 torch = pytest.importorskip("torch")
@@ -182,3 +182,26 @@ def test_batched_argument_errors():
     upload(ctx2, 0, lw)
     with pytest.raises(N.NmoeError):
         ctx2.forward_batched(0, 1, 8, xd, out)
+
+
+def test_t4096_distinct_packs():
+    """Config 2 at its largest size, T = 4096 (t_max 4096), on a layer whose 256 slots all
+    hold different packs: every token's ids against the reference rule on the GPU's
+    logits, and a 256-token sample of outputs against the oracle."""
+    T = 4096
+    lw = distinct_layer(4)
+    ctx = N.Context(quant_bits=4, num_layers=1, t_max=T, device=0)
+    upload(ctx, 0, lw)
+    x, xd = make_x(4096, T, N.DTYPE_BF16)
+    o, idx, w, lg = run(ctx, T, 8, xd, N.DTYPE_BF16)
+    for t in range(T):
+        ridx, rw = O.route_reference(lg[t], 8)
+        np.testing.assert_array_equal(idx[t], ridx)
+        np.testing.assert_allclose(w[t], rw, rtol=2e-6, atol=1e-7)
+    assert np.unique(idx).size == 256          # every slot was read
+    sample = np.random.default_rng(1).choice(T, 256, replace=False)
+    ref = np.stack([O.block_forward(lw, 8, x[t], logits_override=lg[t])["out"] for t in sample])
+    err = rel_l2(o[sample], ref)
+    assert err < OUT_TOL, err
+    assert ctx.device_status() == (N.OK, 0)
+    ctx.close()

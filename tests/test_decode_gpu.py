@@ -9,7 +9,7 @@ import numpy as np
 import pytest
 
 import nmoe_b200 as N
-from nmoe_testutil import bf16_round, rel_l2, upload
+from nmoe_testutil import bf16_round, distinct_layer, rel_l2, upload
 from oracle import oracle as O
 
 torch = pytest.importorskip("torch")
@@ -356,3 +356,23 @@ def test_fp32_expert_path(monkeypatch, name):
         ref = O.block_forward(lw, 8, x, logits_override=lg)
         np.testing.assert_array_equal(idx, ref["idx"])
         assert rel_l2(out, ref["out"]) < 1e-4, rel_l2(out, ref["out"])
+
+
+@pytest.mark.parametrize("bits", [4, 2])
+def test_distinct_packs_in_every_slot(bits):
+    """Every one of the 256 slots holds its own pack: 24 tokens (192 routed picks) must
+    match the oracle, so each unit's copies read the slot the router chose."""
+    lw = distinct_layer(bits)
+    ctx = N.Context(quant_bits=bits, num_layers=1, device=0)
+    upload(ctx, 0, lw)
+    seen = set()
+    for t in range(24):
+        x, xd = make_x(7000 + t, N.DTYPE_BF16)
+        out, idx, w, lg = run_gpu(ctx, 0, 8, xd, N.DTYPE_BF16)
+        ref = O.block_forward(lw, 8, x, logits_override=lg)
+        np.testing.assert_array_equal(idx, ref["idx"])
+        assert rel_l2(out, ref["out"]) < OUT_TOL, rel_l2(out, ref["out"])
+        seen.update(idx.tolist())
+    assert len(seen) > 100
+    assert ctx.device_status() == (N.OK, 0)
+    ctx.close()

@@ -53,6 +53,63 @@ def test_static_forward_matches_context_forward(bits, rdt, xdt):
         assert rel_l2(o2.cpu().numpy(), o1.cpu().numpy()) < 2e-3
 
 
+@pytest.mark.parametrize("bits,rdt,xdt", [(4, N.DTYPE_BF16, N.DTYPE_BF16), (2, N.DTYPE_Q4, N.DTYPE_F32)])
+def test_static_forward_matches_oracle(bits, rdt, xdt):
+    """The static path runs fp32 kernels: held to 1e-4 against the CPU oracle, on the
+    routing the oracle derives from the GPU's logits (ids must agree exactly)."""
+    lw = O.make_layer(5151, bits=bits, router_dtype=rdt, shared_dtype=rdt, distinct_experts=12)
+    ctx = N.Context(quant_bits=bits, num_layers=1, router_dtype=rdt, shared_dtype=rdt, device=0)
+    upload(ctx, 0, lw)
+    experts = torch.from_numpy(lw.experts).cuda()
+    dense = {n: _dev(getattr(lw, n)) for n in ("router", "shared_gate", "shared_up", "shared_down", "shared_gate_vec")}
+    rng = np.random.default_rng(8)
+    for call in range(2):
+        xf = rng.standard_normal(2048, dtype=np.float32)
+        if xdt == N.DTYPE_BF16:
+            xb = O.f32_to_bf16(xf)
+            xf = O.bf16_to_f32(xb)
+            xd = torch.from_numpy(xb.view(np.int16)).cuda()
+        else:
+            xd = torch.from_numpy(xf).cuda()
+        hm = np.random.default_rng(9 + call).standard_normal(2048, dtype=np.float32)
+        k = 8 if call == 0 else 3
+        lg = torch.zeros(256, device="cuda")
+        ctx.route(0, k, xd, x_dtype=xdt, logits_out=lg)
+        out = torch.zeros(2048, device="cuda")
+        idx = torch.zeros(8, dtype=torch.int32, device="cuda")
+        N.forward_static(experts, 256, bits, dense, rdt, rdt, k, xd, out, x_dtype=xdt,
+                         h_mid=torch.from_numpy(hm).cuda(), idx_out=idx)
+        torch.cuda.synchronize()
+        ref = O.block_forward(lw, k, xf, h_mid=hm, logits_override=lg.cpu().numpy())
+        np.testing.assert_array_equal(idx.cpu().numpy()[:k].view(np.uint32), ref["idx"][:k])
+        assert rel_l2(out.cpu().numpy(), ref["out"]) < 1e-4, rel_l2(out.cpu().numpy(), ref["out"])
+        assert N.static_status() == (N.OK, 0)
+
+
+def test_static_status_reports_out_of_range_expert():
+    """A routed id >= num_experts contributes nothing and leaves the device error word set;
+    nmoe_moe_static_status reads it (NMOE_EDEVICE, code 1) and clears it."""
+    lw = O.make_layer(77, bits=4, distinct_experts=8)
+    r = lw.router["weight"].copy()
+    r[250] = r[3]                       # experts 250 and 3 tie at the top: both are picked
+    lw.router = {"dtype": N.DTYPE_BF16, "weight": r}
+    ne = 200                            # ... but only experts 0..199 exist
+    esz = O.expert_size(4)
+    experts = torch.from_numpy(lw.experts[: ne * esz].copy()).cuda()
+    dense = {n: _dev(getattr(lw, n)) for n in ("router", "shared_gate", "shared_up", "shared_down", "shared_gate_vec")}
+    x = O.f32_to_bf16(O.bf16_to_f32(r[3]) * 50.0)
+    xd = torch.from_numpy(x.view(np.int16)).cuda()
+    out = torch.zeros(2048, device="cuda")
+    idx = torch.zeros(8, dtype=torch.int32, device="cuda")
+    N.forward_static(experts, ne, 4, dense, N.DTYPE_BF16, N.DTYPE_BF16, 2, xd, out, idx_out=idx)
+    torch.cuda.synchronize()
+    assert sorted(idx.cpu().numpy()[:2].tolist()) == [3, 250]
+    assert N.static_status() == (N.EDEVICE, 1)
+    assert N.static_status() == (N.OK, 0)
+    assert np.isfinite(out.cpu().numpy()).all()
+    assert N.lib().nmoe_moe_static_scratch_bytes() == 19712
+
+
 def test_static_forward_rejects_k_beyond_scratch():
     x = torch.zeros(2048, dtype=torch.int16, device="cuda")
     out = torch.zeros(2048, device="cuda")
