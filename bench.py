@@ -137,10 +137,59 @@ def profiled_traffic(name: str):
 
 # ------------------------------------------------------------------ workload ----
 
-def build_workload(num_layers: int, bits: int, k: int, router_dtype: int, shared_dtype: int, pool: int, seed: int):
+def host_llc_bytes() -> int:
+    try:
+        v = open("/sys/devices/system/cpu/cpu0/cache/index3/size").read().strip()
+        return int(v[:-1]) * 1024 if v.endswith("K") else int(v[:-1]) * 2**20 if v.endswith("M") else int(v)
+    except Exception:
+        return 0
+
+
+def routing_mass_top20(logits: np.ndarray, k: int) -> float:
+    """Share of the renormalised top-k routing mass (softmax -> top-k -> renormalise, per
+    token) that the 20% most-used experts (51 of 256) receive over the sampled tokens."""
+    z = logits - logits.max(axis=1, keepdims=True)
+    top = np.argpartition(-z, k - 1, axis=1)[:, :k]
+    p = np.exp(np.take_along_axis(z, top, axis=1))
+    p /= p.sum(axis=1, keepdims=True)
+    mass = np.zeros(logits.shape[1])
+    np.add.at(mass, top.ravel(), p.ravel())
+    return float(np.sort(mass)[::-1][: int(0.2 * logits.shape[1])].sum() / mass.sum())
+
+
+def calibrate_router_skew(router_bf16: np.ndarray, k: int, seed: int, tokens: int = 1024):
+    """Config 1's skewed router: logits = x . W_r + b_e, with a seeded per-expert
+    log-popularity b_e = sigma * z_e (z ~ N(0,1)); sigma is bisected so that over `tokens`
+    sampled x ~ N(0,1) the top 20% of experts receive 80% +- 1% of the renormalised routing
+    mass. The bias enters the kernels as router column 2047, with x[2047] = 1."""
+    from oracle import oracle as O
+    rng = np.random.default_rng(seed + 77)
+    z = rng.standard_normal(EXPERTS).astype(np.float32)
+    x = O.bf16_to_f32(O.f32_to_bf16(rng.standard_normal((tokens, HIDDEN), dtype=np.float32)))
+    x[:, HIDDEN - 1] = 1.0
+    w = O.bf16_to_f32(router_bf16).astype(np.float32)
+    w[:, HIDDEN - 1] = 0.0
+    base = x @ w.T
+    lo, hi, sigma, mass = 0.0, 64.0, 0.0, 0.0
+    for _ in range(60):
+        sigma = 0.5 * (lo + hi)
+        b = O.bf16_to_f32(O.f32_to_bf16(sigma * z))
+        mass = routing_mass_top20(base + b[None, :], k)
+        if abs(mass - 0.8) <= 0.005:
+            break
+        lo, hi = (sigma, hi) if mass < 0.8 else (lo, sigma)
+    b16 = O.f32_to_bf16(sigma * z)
+    return b16, {"bias_sigma": sigma, "tau": 1.0, "top20_mass": mass, "tokens": tokens, "k": k,
+                 "rule": "logits = x.W_r + b_e, b_e = sigma*z_e (seeded), x[2047] = 1 carries b_e"}
+
+
+def build_workload(num_layers: int, bits: int, k: int, router_dtype: int, shared_dtype: int, pool: int, seed: int,
+                   skew: bool = False):
     """Seeded synthetic layers: `pool` distinct q4 experts quantised by the restated
     convert_qwen36.py quantiser, placed in the 256 slots of each layer with a per-layer
-    rotation; per-layer bf16 router / shared weights ~N(0, 0.02)."""
+    rotation (each layer's 256 slots are a separate copy in memory); per-layer bf16
+    router / shared weights ~N(0, 0.02). skew: config 1's calibrated router skew
+    (calibrate_router_skew) on every layer; returns (layers, xs, calibration)."""
     from oracle import oracle as O
     rng = np.random.default_rng(seed)
     esz = O.expert_size(bits)
@@ -163,11 +212,32 @@ def build_workload(num_layers: int, bits: int, k: int, router_dtype: int, shared
         layers.append(O.LayerWeights(bits, experts, EXPERTS, dense["router"], dense["shared_gate"],
                                      dense["shared_up"], dense["shared_down"], dense["shared_gate_vec"]))
     xs = O.f32_to_bf16(rng.standard_normal((num_layers, HIDDEN), dtype=np.float32))
-    return layers, xs
+    calib = None
+    if skew:
+        if router_dtype != 1:
+            raise ValueError("the router skew is defined on the bf16 router")
+        bias, calib = calibrate_router_skew(layers[0].router["weight"], k, seed)
+        for lw in layers:
+            r = lw.router["weight"].copy()
+            r[:, HIDDEN - 1] = bias
+            lw.router = {"dtype": 1, "weight": r}
+        xs[:, HIDDEN - 1] = O.f32_to_bf16(np.ones(1, np.float32))[0]
+        # the mass with the bias as the kernels see it (bf16 column, x[2047] = 1), fresh tokens
+        xt = O.bf16_to_f32(O.f32_to_bf16(np.random.default_rng(seed + 78).standard_normal((1024, HIDDEN),
+                                                                                       dtype=np.float32)))
+        xt[:, HIDDEN - 1] = 1.0
+        calib["top20_mass_checked"] = routing_mass_top20(xt @ O.bf16_to_f32(layers[0].router["weight"]).T, k)
+    return layers, xs, calib
 
 
-def cpu_baseline_sample(layers, xs, k, seconds: float):
-    """Oracle block forward (all host threads) on a bounded sample of the same calls."""
+CPU_LAYERS = 8   # layers the CPU sample rotates over: 8 x 453 MB of expert slots >> host LLC
+
+
+def cpu_sample(layers, xs, k, seconds: float):
+    """The oracle's block forward (all host threads) over batch-1 calls rotating through
+    `layers` (each with its own 256 expert slots in memory, so that the working set is far
+    above the host's last-level cache), for about `seconds`. Returns (calls/s, threads,
+    calls, seconds). The GPU arm's cpu_baseline and the reference arm both use it."""
     from oracle import oracle as O
     L = O.lib()
     n, t0 = 0, time.perf_counter()
@@ -181,6 +251,13 @@ def cpu_baseline_sample(layers, xs, k, seconds: float):
     return n / el, L.orc_get_threads(), n, el
 
 
+def cpu_sample_text(n_layers, n, el, bits, k):
+    llc = host_llc_bytes()
+    return (f"{n} batch-1 layer calls in {el:.1f}s rotating over {n_layers} layers (q{bits}, k={k}, each layer "
+            f"its own 256 expert slots: {n_layers * 256 * (1769472 if bits == 4 else 983040) / 2**20:.0f} MiB of "
+            f"expert memory; host LLC {llc / 2**20:.0f} MiB), oracle port of the reference block, OpenMP")
+
+
 # ---------------------------------------------------------------- reference ----
 
 def run_reference(args, rank, world):
@@ -188,14 +265,14 @@ def run_reference(args, rank, world):
         return None
     from oracle import oracle as O
     O.build()
-    n_layers = 2
-    layers, xs = build_workload(n_layers, args.bits, args.k, 1, 1, pool=8, seed=args.seed)
-    calls_per_step = 4
+    n_layers = CPU_LAYERS
+    skew = args.bits == 2
+    layers, xs, calib = build_workload(n_layers, args.bits, args.k, 1, 1, pool=args.pool, seed=args.seed, skew=skew)
     k = args.k
 
-    def step():
-        for j in range(calls_per_step):
-            O.block_forward(layers[j % n_layers], k, O.bf16_to_f32(xs[j % n_layers]))
+    def step():   # one step = one call per layer, as in the GPU arm's step over its layers
+        for l in range(n_layers):
+            O.block_forward(layers[l], k, O.bf16_to_f32(xs[l]))
 
     for _ in range(args.warmup):
         step()
@@ -203,21 +280,29 @@ def run_reference(args, rank, world):
     for _ in range(args.steps):
         step()
     el = time.perf_counter() - t0
-    value = args.steps * calls_per_step / el
+    calls = args.steps * n_layers
+    value = calls / el
     cores = O.lib().orc_get_threads()
-    sample = (f"{calls_per_step} batch-1 layer calls per step (q{args.bits} experts, k={k}, bf16 router/shared), "
-              f"CPU oracle port of the reference block, OpenMP over output rows")
-    return {
+    res = {
         "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded bf16 ~N(0,0.02) weights quantised by the reference quantiser rule)",
-        "config": {"workload": f"config{0 if args.bits == 4 else 1} batch-1 decode, q{args.bits} experts, k={k}, "
-                               "bf16 router/shared, x bf16",
-                   "layers_in_sample": n_layers},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "config": {"workload": workload_name(args.bits, n_layers, k), "layers": n_layers, "k": k,
+                   "step": f"{n_layers} layer calls (one token through {n_layers} MoE blocks)"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": cpu_sample_text(n_layers, calls, el, args.bits, k)},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if calib is not None:
+        res["config"]["router_skew"] = calib
+    return res
+
+
+def workload_name(bits, L, k):
+    return (f"config{0 if bits == 4 else 1} batch-1 decode: {L} layers x 256 q{bits} experts resident, k={k}, "
+            "bf16 router/shared/gate-vector, x bf16 [1,2048]"
+            + ("; router skewed (top 20% of experts get 80% of routing mass)" if bits == 2 else ""))
 
 
 # ------------------------------------------------------------------ batched ----
@@ -239,7 +324,7 @@ def run_batched(args, rank, world, local_rank):
     bits, k, rdt, sdt = 4, 8, N.DTYPE_BF16, N.DTYPE_BF16
     T, L = args.tokens, args.batched_layers
     # one model on every rank: with expert parallelism each rank holds a slice of it
-    layers, _ = build_workload(L, bits, k, rdt, sdt, pool=args.pool, seed=args.seed)
+    layers, _, _ = build_workload(L, bits, k, rdt, sdt, pool=args.pool, seed=args.seed)
     uid = None
     if world > 1:   # experts sharded 256/world per rank, tokens exchanged by NCCL
         obj = [N.nccl_unique_id() if rank == 0 else None]
@@ -411,14 +496,15 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.set_device(dev)
     bits, k, rdt, sdt = args.bits, args.k, N.DTYPE_BF16, N.DTYPE_BF16
     L = args.layers
-    layers, xs_h = build_workload(L, bits, k, rdt, sdt, pool=args.pool, seed=args.seed + rank)
+    layers, xs_h, calib = build_workload(L, bits, k, rdt, sdt, pool=args.pool, seed=args.seed + rank, skew=bits == 2)
     flags = N.FLAG_PREFETCH_NEXT_LAYER if args.prefetch else 0
     ctx = N.Context(quant_bits=bits, num_layers=L, router_dtype=rdt, shared_dtype=sdt, device=dev, flags=flags)
     for l, lw in enumerate(layers):
         ctx.load_layer(l, lw.experts)
         ctx.set_dense(l, lw.router, lw.shared_gate, lw.shared_up, lw.shared_down, lw.shared_gate_vec)
-    cpu_layers = layers[:2]
-    for lw in layers[2:]:
+    cpu_layers = layers[:CPU_LAYERS]
+    fp32_layers = layers[:CPU_LAYERS]
+    for lw in layers[CPU_LAYERS:]:
         lw.experts = None
     del layers
 
@@ -496,6 +582,37 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_value = e2e_steps * L * world / float(te.item())
 
+    # the fp32 routed-expert path (NMOE_FLAG_EXPERT_FP32), timed the same way on the first
+    # CPU_LAYERS layers, reported beside the default half2 path
+    fp32 = None
+    if rank == 0:
+        L8 = len(fp32_layers)
+        cf = N.Context(quant_bits=bits, num_layers=L8, router_dtype=rdt, shared_dtype=sdt, device=dev,
+                       flags=N.FLAG_EXPERT_FP32)
+        for l, lw in enumerate(fp32_layers):
+            cf.load_layer(l, lw.experts)
+            cf.set_dense(l, lw.router, lw.shared_gate, lw.shared_up, lw.shared_down, lw.shared_gate_vec)
+        gf = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gf, stream=stream):
+            for l in range(L8):
+                cf.forward(l, k, xs[l], outs[l], x_dtype=N.DTYPE_BF16, stream=torch.cuda.current_stream().cuda_stream)
+        for _ in range(3):
+            gf.replay()
+        torch.cuda.synchronize()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = max(5, args.steps)
+        f0.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(reps):
+                gf.replay()
+        f1.record(stream)
+        torch.cuda.synchronize()
+        fms = f0.elapsed_time(f1)
+        fp32 = {"value": reps * L8 / (fms / 1e3), "unit": UNIT, "layers": L8,
+                "dtype": "fp32 products and accumulation (q weights, fp32 x and activations)"}
+        del gf
+        cf.close()
+
     # correctness of the timed outputs (layer 0 vs oracle, using the GPU's own routing)
     lg = torch.zeros(256, dtype=torch.float32, device=f"cuda:{dev}")
     ctx.route(0, k, xs[0], x_dtype=N.DTYPE_BF16, logits_out=lg)
@@ -515,34 +632,39 @@ def run_ours(args, rank, world, local_rank):
         launches_per_call = 1   # one persistent kernel per layer call
         cpu = None
         if world == 1:
-            v, cores, n, el = cpu_baseline_sample(cpu_layers, xs_h, k, args.cpu_seconds)
+            v, cores, n, el = cpu_sample(cpu_layers, xs_h, k, args.cpu_seconds)
             cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
-                   "sample": f"{n} batch-1 layer calls of the same config in {el:.1f}s (oracle, OpenMP)"}
+                   "sample": cpu_sample_text(len(cpu_layers), n, el, bits, k)}
         result = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": f"bf16/q{bits} in, f32 accumulate",
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": (f"routed experts: q{bits} weights x fp16-scaled x / activations, half2 partial sums over "
+                      f"{4 if bits == 4 else 8} products flushed to fp32; router, shared expert, combine fp32"),
             "data": "synthetic (seeded bf16 ~N(0,0.02) weights quantised by the reference quantiser rule; "
                     f"{args.pool} distinct expert packs placed in 256 slots per layer)",
-            "config": {"workload": (f"config0 batch-1 decode: {L} layers x 256 q4 experts resident, k={k}, "
-                                    if bits == 4 else
-                                    f"config1 batch-1 decode: {L} layers x 256 q2 experts resident, k={k}, ")
-                                   + "bf16 router/shared/gate-vector, x bf16 [1,2048]",
+            "config": {"workload": workload_name(bits, L, k),
                        "layers": L, "k": k, "step": f"{L} layer calls (one token through {L} MoE blocks)",
-                       "l2": "inputs larger than L2 (a step touches ~860 MB of weights)",
+                       "l2": f"inputs larger than L2: a step reads {L * abytes / 1e6:.0f} MB of weights "
+                             f"({L} layers x {abytes / 1e6:.1f} MB) against a 126 MB L2; no flush",
                        "parallelism": "replicas only" if world > 1 else "single GPU",
                        "timing": "CUDA graph of one step, CUDA events, max over ranks",
                        "next_layer_prefetch": bool(args.prefetch)},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk, "unit": "GB/s", "frac": achieved / pk,
                          "peak_kind": pk_kind, "algorithmic_bytes_per_launch": abytes,
-                         "traffic": profiled_traffic("decode_fused_cfg0") if (bits, k) == (4, 8) else None},
+                         "traffic": profiled_traffic("decode_fused_cfg0") if (bits, k) == (4, 8) else None,
+                         "traffic_source": "ncu dram__bytes_read+write of this kernel on this config, copied from "
+                                           "profiles/decode_fused_cfg0.md (not measured in this run)"},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": L * HIDDEN * 2,
                     "d2h_bytes_per_step": L * HIDDEN * 4},
             "gpu_launches": args.steps * L * launches_per_call,
             "clocks": clk,
             "check": {"rel_l2_layer0": rel},
+            "expert_fp32_path": fp32,
         }
+        if calib is not None:
+            result["config"]["router_skew"] = calib
     ctx.close()
     return result
 
