@@ -592,10 +592,11 @@ def run_ours(args, rank, world, local_rank):
         for l, lw in enumerate(fp32_layers):
             cf.load_layer(l, lw.experts)
             cf.set_dense(l, lw.router, lw.shared_gate, lw.shared_up, lw.shared_down, lw.shared_gate_vec)
+        outs_f = torch.zeros((L8, HIDDEN), dtype=torch.float32, device=f"cuda:{dev}")   # keeps `outs` the timed path's
         gf = torch.cuda.CUDAGraph()
         with torch.cuda.graph(gf, stream=stream):
             for l in range(L8):
-                cf.forward(l, k, xs[l], outs[l], x_dtype=N.DTYPE_BF16, stream=torch.cuda.current_stream().cuda_stream)
+                cf.forward(l, k, xs[l], outs_f[l], x_dtype=N.DTYPE_BF16, stream=torch.cuda.current_stream().cuda_stream)
         for _ in range(3):
             gf.replay()
         torch.cuda.synchronize()
