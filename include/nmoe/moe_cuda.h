@@ -168,12 +168,20 @@ int nmoe_moe_route(nmoe_moe_ctx *ctx, int layer, int k, const void *x, int x_dty
 /* T tokens (prefill / batched decode) through one layer: x device [T][2048] (bf16 or
  * f32), h_mid device fp32 [T][2048] or NULL, out device [T][2048] in out_dtype
  * (F32 or BF16), idx_out/w_out device [T][8] optional. T <= t_max. With world_size > 1
- * every rank passes its own T tokens; experts are sharded num_experts/world_size per
- * rank and tokens travel by NCCL all-to-all. No reference counterpart (the reference
- * runs prefill token by token, src/runtime.m:3816). */
+ * every rank passes its own T tokens (0 allowed) and every rank must make the same calls
+ * in the same order; experts are sharded num_experts/world_size per rank and token rows
+ * travel by NVLink peer stores between the ranks' mapped buffers, on the stream, with no
+ * host synchronisation (t_max and k_max must be equal on all ranks). No reference
+ * counterpart (the reference runs prefill token by token, src/runtime.m:3816). */
 int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int k, const void *x, int x_dtype,
                              const float *h_mid, void *out, int out_dtype, uint32_t *idx_out,
                              float *w_out, void *stream);
+
+/* Diagnostics: device time (ms) of the last expert-parallel call's two exchanges:
+ * ms[0] = dispatch of the token rows + wait for every source's rows, ms[1] = return of the
+ * down outputs + wait for every owner's returns. Needs world_size > 1 and NMOE_EP_TIMING=1
+ * in the environment at create. Synchronises on the last call. No reference counterpart. */
+int nmoe_moe_debug_ep_times(nmoe_moe_ctx *ctx, float *ms);
 
 /* Expert parallelism: fill `out` (>= 128 bytes) with a fresh NCCL unique id. One rank
  * calls it and hands the bytes to every rank's nmoe_moe_config.nccl_unique_id. No

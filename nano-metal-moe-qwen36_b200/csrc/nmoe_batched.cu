@@ -62,16 +62,42 @@ struct BatchedState {
 };
 
 // Expert parallelism (world_size > 1): this rank holds experts [expert_lo, expert_lo +
-// n_local) and exchanges token rows with the other ranks by NCCL send/recv.
+// n_local) and exchanges token rows with the other ranks by NVLink peer stores into a
+// symmetric arena that every rank maps (CUDA IPC). Per call, on the device only:
+//   dispatch: rows go into slab `rank` of each destination's xr (fixed capacity C =
+//             t_max * k_max rows, so no sizes travel to the host first), with the counts
+//             per local expert and this rank's segment offset; a flag with the call's tag
+//             follows the rows;
+//   wait:     the receiver waits (bounded) for every source's flag;
+//   compute:  the grouped GEMMs read the slabs (groups (source, local expert));
+//   return:   down outputs go back into the source's yret, at the positions the rows left
+//             from; a second flag follows; the source waits for every receiver's flag and
+//             combines.
+// Calls alternate between two sets of buffers: a rank writes set (call & 1) of a peer only
+// after that peer returned this rank's rows of the call two back, so nothing overwrites
+// data still being read.
+constexpr int kEpMaxWorld = 8;
+struct EpLayout {              // offsets inside each rank's arena
+    size_t flags;              // arrive[kEpMaxWorld], ret[kEpMaxWorld]: u32, 64 bytes apart
+    size_t rcnt;               // [2][W][n_local] int: rows per (source, local expert)
+    size_t rmeta;              // [2][W] int: the source's position of its first row here
+    size_t xr;                 // [2][W][C][2048] bf16: received rows, slab per source
+    size_t yret;               // [2][C][2048] bf16: this rank's rows' down outputs, position order
+    size_t total;
+};
 struct EpState {
-    ncclComm_t comm = nullptr;
+    ncclComm_t comm = nullptr;   // set-up only (handle exchange, barriers)
     int world = 1, rank = 0;
-    size_t r_cap = 0;            // rows this rank can receive: world * t_max * k_max
-    uint16_t *xr = nullptr;      // [r_cap][2048] received token rows, (source rank, local expert) order
-    uint16_t *yr = nullptr;      // [r_cap][2048] their down outputs
-    int *rcnt = nullptr;         // [world][n_local] rows received per (source, local expert)
-    int *h_cnt = nullptr;        // pinned [256] this rank's counts per global expert
-    int *h_rcnt = nullptr;       // pinned [world * n_local]
+    size_t C = 0;                // slab rows: t_max * k_max
+    EpLayout L{};
+    uint8_t *arena = nullptr;    // this rank's arena (exported)
+    uint8_t *peer[kEpMaxWorld] = {};   // every rank's arena as mapped here (peer[rank] = arena)
+    uint8_t **d_peer = nullptr;  // device copy of peer[]
+    uint16_t *yr = nullptr;      // [W * C][2048] down outputs of the received rows (slab order)
+    unsigned *done = nullptr;    // [2] grid completion counters (dispatch, return)
+    uint32_t call = 0;           // calls so far; the tag of a call is call + 1
+    bool timing = false;         // NMOE_EP_TIMING=1: events around the exchanges
+    cudaEvent_t ev[4] = {};
 };
 
 }  // namespace nmoe
@@ -331,6 +357,131 @@ __global__ void k_combine(const uint16_t *y, const float *w, const int *inv, con
     }
 }
 
+// ------------------------------------------------------ expert parallelism ----
+
+// Exclusive prefix over the 256 per-expert counts (256 threads): off[e] = sum_{e' < e} cnt[e'].
+__device__ __forceinline__ void block_prefix256(const int *cnt, int *off, int *wsum) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int c = cnt[tid];
+    int x = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) wsum[warp] = x;
+    __syncthreads();
+    int base = 0;
+    for (int i = 0; i < warp; ++i) base += wsum[i];
+    off[tid] = base + x - c;
+    __syncthreads();
+}
+
+__device__ __forceinline__ void st_release_sys_u32(uint32_t *p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+struct EpArgs {
+    uint8_t *const *peer;        // arenas of every rank
+    EpLayout L;
+    int world, rank, n_local, set;
+    size_t C;
+    uint32_t tag;
+    unsigned *done;
+};
+
+// The last block of a grid to finish (after every block's stores, made visible system-wide)
+// raises flag `which` (0 arrive, 1 ret) of this rank in every peer's arena.
+__device__ __forceinline__ void ep_signal_last(const EpArgs &a, int which, unsigned *done) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        if (atomicAdd(done, 1u) == gridDim.x - 1) {
+            *done = 0;
+            __threadfence_system();
+            for (int p = 0; p < a.world; ++p)
+                st_release_sys_u32(reinterpret_cast<uint32_t *>(a.peer[p] + a.L.flags) + (which * kEpMaxWorld + a.rank) * 16,
+                                   a.tag);
+        }
+    }
+}
+
+// Dispatch: block b < T*k copies row (t, s) = (b / k, b % k) of xh into slab `rank` of the
+// owner of its expert; blocks b < world also write that destination's counts and this
+// rank's segment offset. Grid: max(T*k, world) blocks of 256 threads.
+__global__ void __launch_bounds__(256) k_ep_dispatch(EpArgs a, const uint16_t *xh, const uint32_t *idx,
+                                                     const int *inv, const int *cnt, int T, int k) {
+    __shared__ int off[kExperts];
+    __shared__ int wsum[8];
+    block_prefix256(cnt, off, wsum);
+    const int b = blockIdx.x, tid = threadIdx.x, nl = a.n_local;
+    if (b < T * k) {
+        const int t = b / k, s = b - t * k;
+        const int pos = inv[(size_t)t * kMaxK + s];
+        if (pos >= 0) {
+            const int p = (int)idx[(size_t)t * kMaxK + s] / nl;
+            const size_t row = ((size_t)a.set * a.world + a.rank) * a.C + (size_t)(pos - off[p * nl]);
+            uint4 *dst = reinterpret_cast<uint4 *>(a.peer[p] + a.L.xr) + row * (kHidden / 8);
+            dst[tid] = reinterpret_cast<const uint4 *>(xh + (size_t)t * kHidden)[tid];
+        }
+    }
+    if (b < a.world) {
+        int *rc = reinterpret_cast<int *>(a.peer[b] + a.L.rcnt) + ((size_t)a.set * a.world + a.rank) * nl;
+        if (tid < nl) rc[tid] = cnt[b * nl + tid];
+        if (tid == 0) reinterpret_cast<int *>(a.peer[b] + a.L.rmeta)[a.set * a.world + a.rank] = off[b * nl];
+    }
+    ep_signal_last(a, 0, a.done);
+}
+
+// Wait (bounded) until every rank's flag `which` in this rank's arena carries the tag.
+__global__ void k_ep_wait(EpArgs a, int which, int *err, uint64_t timeout_ns) {
+    const int p = threadIdx.x;
+    if (p >= a.world) return;
+    const uint32_t *f = reinterpret_cast<const uint32_t *>(a.peer[a.rank] + a.L.flags) + (which * kEpMaxWorld + p) * 16;
+    const uint64_t deadline = globaltimer_ns() + timeout_ns;
+    for (uint32_t it = 0;; ++it) {
+        if ((int)(ld_acquire_sys_u32(f) - a.tag) >= 0) return;
+        if (it >= kMaxSpins || globaltimer_ns() > deadline) {
+            atomicCAS(err, 0, kErrTimeout);
+            return;
+        }
+    }
+}
+
+// Return: every received row's down output (yr, slab order) goes back into its source's
+// yret at the source's position; then the ret flags. Grid-stride over the received rows.
+__global__ void __launch_bounds__(256) k_ep_return(EpArgs a, const uint16_t *yr) {
+    __shared__ int tot[kEpMaxWorld + 1];
+    __shared__ int meta[kEpMaxWorld];
+    const int tid = threadIdx.x, nl = a.n_local;
+    const int *rc = reinterpret_cast<const int *>(a.peer[a.rank] + a.L.rcnt) + (size_t)a.set * a.world * nl;
+    if (tid < a.world) {
+        int n = 0;
+        for (int j = 0; j < nl; ++j) n += rc[tid * nl + j];
+        tot[tid + 1] = n;
+        meta[tid] = reinterpret_cast<const int *>(a.peer[a.rank] + a.L.rmeta)[a.set * a.world + tid];
+    }
+    if (tid == 0) tot[0] = 0;
+    __syncthreads();
+    if (tid == 0)
+        for (int r = 0; r < a.world; ++r) tot[r + 1] += tot[r];
+    __syncthreads();
+    for (int q = blockIdx.x; q < tot[a.world]; q += gridDim.x) {
+        int r = 0;
+        while (q >= tot[r + 1]) ++r;
+        const int i = q - tot[r];
+        const uint4 *src = reinterpret_cast<const uint4 *>(yr + ((size_t)r * a.C + i) * kHidden);
+        uint4 *dst = reinterpret_cast<uint4 *>(a.peer[r] + a.L.yret) + ((size_t)a.set * a.C + meta[r] + i) * (kHidden / 8);
+        dst[tid] = src[tid];
+    }
+    ep_signal_last(a, 1, a.done + 1);
+}
+
 // ------------------------------------------------------------- host side ----
 
 namespace {
@@ -526,12 +677,16 @@ int nmoe_batched_init(nmoe_moe_ctx *ctx) {
     const int W = ctx->cfg.world_size;
     size_t act_rows = T * 9;
     if (W > 1) {
+        if (W > kEpMaxWorld || kExperts / W < 8) {
+            nmoe_ctx_set_error(ctx, "expert parallelism supports 2..%d ranks", kEpMaxWorld);
+            return NMOE_EINVAL;
+        }
         EpState *E = new (std::nothrow) EpState();
         if (E == nullptr) return NMOE_ENOMEM;
         ctx->ep = E;
         E->world = W;
         E->rank = ctx->cfg.rank;
-        E->r_cap = (size_t)W * T * ctx->cfg.k_max;
+        E->C = T * (size_t)ctx->cfg.k_max;
         ncclUniqueId id;
         memcpy(&id, ctx->cfg.nccl_unique_id, sizeof id);
         const ncclResult_t nr = ncclCommInitRank(&E->comm, W, id, E->rank);
@@ -540,15 +695,90 @@ int nmoe_batched_init(nmoe_moe_ctx *ctx) {
             nmoe_ctx_set_error(ctx, "ncclCommInitRank: %s", ncclGetErrorString(nr));
             return NMOE_ENCCL;
         }
-        act_rows = E->r_cap + T;
-        e = cudaMalloc(&E->xr, E->r_cap * kHidden * 2);
-        if (e == cudaSuccess) e = cudaMalloc(&E->yr, E->r_cap * kHidden * 2);
-        if (e == cudaSuccess) e = cudaMalloc(&E->rcnt, (size_t)kExperts * 4);
-        if (e == cudaSuccess) e = cudaMallocHost(&E->h_cnt, (size_t)kExperts * 4);
-        if (e == cudaSuccess) e = cudaMallocHost(&E->h_rcnt, (size_t)kExperts * 4);
+        const int nl = ctx->n_local;
+        auto al256 = [](size_t v) { return (v + 255) & ~size_t(255); };
+        EpLayout &L = E->L;
+        L.flags = 0;
+        L.rcnt = al256(2 * kEpMaxWorld * 64);
+        L.rmeta = al256(L.rcnt + (size_t)2 * W * nl * 4);
+        L.xr = al256(L.rmeta + (size_t)2 * W * 4);
+        L.yret = al256(L.xr + (size_t)2 * W * E->C * kHidden * 2);
+        L.total = al256(L.yret + (size_t)2 * E->C * kHidden * 2);
+        act_rows = (size_t)W * E->C + T;
+        e = cudaMalloc(&E->arena, L.total);
+        if (e == cudaSuccess) e = cudaMemset(E->arena, 0, L.xr);   // flags, counts, offsets
+        if (e == cudaSuccess) e = cudaMalloc(&E->yr, (size_t)W * E->C * kHidden * 2);
+        if (e == cudaSuccess) e = cudaMalloc(&E->done, 2 * sizeof(unsigned));
+        if (e == cudaSuccess) e = cudaMemset(E->done, 0, 2 * sizeof(unsigned));
+        if (e == cudaSuccess) e = cudaMalloc(&E->d_peer, kEpMaxWorld * sizeof(uint8_t *));
         if (e != cudaSuccess) {
             nmoe_ctx_set_error(ctx, "expert-parallel buffers: %s", cudaGetErrorString(e));
             return e == cudaErrorMemoryAllocation ? NMOE_ENOMEM : NMOE_ECUDA;
+        }
+        // Every rank's (t_max, k_max, n_local) and arena handle, gathered once: the slabs have
+        // one capacity on all ranks, so the sizes must agree (checked here, on every rank).
+        struct Rec {
+            int t_max, k_max, n_local, device;
+            cudaIpcMemHandle_t h;
+        };
+        Rec mine{};
+        mine.t_max = tm;
+        mine.k_max = ctx->cfg.k_max;
+        mine.n_local = nl;
+        mine.device = ctx->device;
+        if ((e = cudaIpcGetMemHandle(&mine.h, E->arena)) != cudaSuccess) {
+            nmoe_ctx_set_error(ctx, "cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
+            return NMOE_ECUDA;
+        }
+        Rec *d_recs = nullptr;
+        std::vector<Rec> recs(W);
+        e = cudaMalloc(&d_recs, sizeof(Rec) * W);
+        if (e == cudaSuccess) e = cudaMemcpy(d_recs + E->rank, &mine, sizeof mine, cudaMemcpyHostToDevice);
+        ncclResult_t gr = ncclSuccess;
+        if (e == cudaSuccess) gr = ncclAllGather(d_recs + E->rank, d_recs, sizeof(Rec), ncclChar, E->comm, 0);
+        if (e == cudaSuccess && gr == ncclSuccess) e = cudaMemcpy(recs.data(), d_recs, sizeof(Rec) * W, cudaMemcpyDeviceToHost);
+        if (d_recs) cudaFree(d_recs);
+        if (gr != ncclSuccess || e != cudaSuccess) {
+            nmoe_ctx_set_error(ctx, "expert-parallel set-up exchange: %s",
+                               gr != ncclSuccess ? ncclGetErrorString(gr) : cudaGetErrorString(e));
+            return gr != ncclSuccess ? NMOE_ENCCL : NMOE_ECUDA;
+        }
+        for (int p = 0; p < W; ++p)
+            if (recs[p].t_max != tm || recs[p].k_max != ctx->cfg.k_max || recs[p].n_local != nl) {
+                nmoe_ctx_set_error(ctx, "rank %d has t_max=%d k_max=%d, rank %d t_max=%d k_max=%d: expert parallelism "
+                                   "needs the same t_max and k_max on every rank", p, recs[p].t_max, recs[p].k_max,
+                                   E->rank, tm, ctx->cfg.k_max);
+                return NMOE_EINVAL;
+            }
+        for (int p = 0; p < W; ++p) {
+            if (p == E->rank) {
+                E->peer[p] = E->arena;
+                continue;
+            }
+            void *ptr = nullptr;
+            if ((e = cudaIpcOpenMemHandle(&ptr, recs[p].h, cudaIpcMemLazyEnablePeerAccess)) != cudaSuccess) {
+                nmoe_ctx_set_error(ctx, "cudaIpcOpenMemHandle (rank %d): %s", p, cudaGetErrorString(e));
+                return NMOE_ECUDA;
+            }
+            E->peer[p] = static_cast<uint8_t *>(ptr);
+        }
+        if ((e = cudaMemcpy(E->d_peer, E->peer, kEpMaxWorld * sizeof(uint8_t *), cudaMemcpyHostToDevice)) != cudaSuccess) {
+            nmoe_ctx_set_error(ctx, "expert-parallel peers: %s", cudaGetErrorString(e));
+            return NMOE_ECUDA;
+        }
+        if (const char *t = getenv("NMOE_EP_TIMING")) E->timing = atoi(t) != 0;
+        if (E->timing)
+            for (auto &ev : E->ev) cudaEventCreate(&ev);
+        // every rank has mapped every arena before any rank's first dispatch writes into one
+        int *d_one = nullptr;
+        e = cudaMalloc(&d_one, sizeof(int));
+        if (e == cudaSuccess) e = cudaMemset(d_one, 0, sizeof(int));
+        if (e == cudaSuccess) gr = ncclAllReduce(d_one, d_one, 1, ncclInt32, ncclSum, E->comm, 0);
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        if (d_one) cudaFree(d_one);
+        if (gr != ncclSuccess || e != cudaSuccess) {
+            nmoe_ctx_set_error(ctx, "expert-parallel set-up barrier failed");
+            return gr != ncclSuccess ? NMOE_ENCCL : NMOE_ECUDA;
         }
     }
     struct { void **p; size_t bytes; } al[] = {
@@ -584,12 +814,25 @@ void nmoe_batched_destroy(nmoe_moe_ctx *ctx) {
     delete B;
     ctx->batched = nullptr;
     if (EpState *E = ctx->ep) {
+        // no rank may still write into this arena: a barrier over all ranks before unmapping
+        if (E->comm && E->d_peer) {
+            int *d_one = nullptr;
+            if (cudaMalloc(&d_one, sizeof(int)) == cudaSuccess) {
+                cudaMemset(d_one, 0, sizeof(int));
+                ncclAllReduce(d_one, d_one, 1, ncclInt32, ncclSum, E->comm, 0);
+                cudaDeviceSynchronize();
+                cudaFree(d_one);
+            }
+        }
+        for (int p = 0; p < E->world; ++p)
+            if (E->peer[p] && p != E->rank) cudaIpcCloseMemHandle(E->peer[p]);
         if (E->comm) ncclCommDestroy(E->comm);
-        if (E->xr) cudaFree(E->xr);
+        if (E->arena) cudaFree(E->arena);
         if (E->yr) cudaFree(E->yr);
-        if (E->rcnt) cudaFree(E->rcnt);
-        if (E->h_cnt) cudaFreeHost(E->h_cnt);
-        if (E->h_rcnt) cudaFreeHost(E->h_rcnt);
+        if (E->done) cudaFree(E->done);
+        if (E->d_peer) cudaFree(E->d_peer);
+        for (auto ev : E->ev)
+            if (ev) cudaEventDestroy(ev);
         delete E;
         ctx->ep = nullptr;
     }
@@ -713,64 +956,43 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
             k_route<<<(T + kRouteWarps - 1) / kRouteWarps, kRouteWarps * 32, 0, st>>>(a);
             k_scatter<<<(T * k + 255) / 256, 256, 0, st>>>(B->idx, B->rank, B->cnt, T, k, a.expert_lo, a.n_local,
                                                            B->perm, B->inv);
-            k_gather_rows<<<T * k, 256, 0, st>>>(B->xh, B->perm, T, k, B->xp);
+            if (E == nullptr) k_gather_rows<<<T * k, 256, 0, st>>>(B->xh, B->perm, T, k, B->xp);
         }
     }
     int shared_base = T * k;
 
-    // 3b. expert parallelism: send each rank the rows routed to its experts
-    std::vector<long> soff, scnt, roff, rcnt_s;
+    // 3b. expert parallelism: rows into the owners' slabs (peer stores), then wait for
+    // every source's rows (all on the stream: no host synchronisation)
+    EpArgs ea{};
     if (E != nullptr) {
-        const int W = E->world, nl = ctx->n_local;
-        ncclResult_t nr = ncclGroupStart();
-        for (int p = 0; p < W && nr == ncclSuccess; ++p) {
-            nr = ncclSend(B->cnt + p * nl, nl, ncclInt32, p, E->comm, st);
-            if (nr == ncclSuccess) nr = ncclRecv(E->rcnt + p * nl, nl, ncclInt32, p, E->comm, st);
-        }
-        if (nr == ncclSuccess) nr = ncclGroupEnd();
-        if (nr != ncclSuccess) {
-            nmoe_ctx_set_error(ctx, "count exchange: %s", ncclGetErrorString(nr));
-            return NMOE_ENCCL;
-        }
-        cudaMemcpyAsync(E->h_cnt, B->cnt, kExperts * 4, cudaMemcpyDeviceToHost, st);
-        cudaMemcpyAsync(E->h_rcnt, E->rcnt, (size_t)W * nl * 4, cudaMemcpyDeviceToHost, st);
-        if ((e = cudaStreamSynchronize(st)) != cudaSuccess) {   // NCCL needs the sizes on the host
-            nmoe_ctx_set_error(ctx, "count exchange: %s", cudaGetErrorString(e));
+        ea.peer = E->d_peer;
+        ea.L = E->L;
+        ea.world = E->world;
+        ea.rank = E->rank;
+        ea.n_local = ctx->n_local;
+        ea.set = (int)(E->call & 1u);
+        ea.C = E->C;
+        ea.tag = E->call + 1u;
+        ea.done = E->done;
+        ++E->call;
+        if (E->timing) cudaEventRecord(E->ev[0], st);
+        k_ep_dispatch<<<std::max(T * k, E->world), 256, 0, st>>>(ea, B->xh, B->idx, B->inv, B->cnt, T, k);
+        k_ep_wait<<<1, 32, 0, st>>>(ea, 0, ctx->d_err, B->timeout_ns);
+        if (E->timing) cudaEventRecord(E->ev[1], st);
+        if ((e = cudaGetLastError()) != cudaSuccess) {
+            nmoe_ctx_set_error(ctx, "token dispatch: %s", cudaGetErrorString(e));
             return NMOE_ECUDA;
         }
-        soff.assign(W + 1, 0);
-        roff.assign(W + 1, 0);
-        scnt.assign(W, 0);
-        rcnt_s.assign(W, 0);
-        for (int p = 0; p < W; ++p) {
-            for (int j = 0; j < nl; ++j) {
-                scnt[p] += E->h_cnt[p * nl + j];
-                rcnt_s[p] += E->h_rcnt[p * nl + j];
-            }
-            soff[p + 1] = soff[p] + scnt[p];
-            roff[p + 1] = roff[p] + rcnt_s[p];
-        }
-        if ((size_t)roff[W] > E->r_cap) {
-            nmoe_ctx_set_error(ctx, "received %ld rows, capacity %zu", roff[W], E->r_cap);
-            return NMOE_ESIZE;
-        }
-        nr = ncclGroupStart();
-        for (int p = 0; p < W && nr == ncclSuccess; ++p) {
-            if (scnt[p]) nr = ncclSend(B->xp + soff[p] * kHidden, (size_t)scnt[p] * kHidden * 2, ncclChar, p, E->comm, st);
-            if (nr == ncclSuccess && rcnt_s[p])
-                nr = ncclRecv(E->xr + roff[p] * kHidden, (size_t)rcnt_s[p] * kHidden * 2, ncclChar, p, E->comm, st);
-        }
-        if (nr == ncclSuccess) nr = ncclGroupEnd();
-        if (nr != ncclSuccess) {
-            nmoe_ctx_set_error(ctx, "token dispatch: %s", ncclGetErrorString(nr));
-            return NMOE_ENCCL;
-        }
-        shared_base = (int)roff[W];
+        shared_base = (int)((size_t)E->world * E->C);
     }
     const int n_groups = E ? E->world * ctx->n_local : ctx->n_local;
-    const int *gcnt = E ? E->rcnt : B->cnt;
+    const int *gcnt = E ? reinterpret_cast<const int *>(E->arena + E->L.rcnt) + (size_t)ea.set * E->world * ctx->n_local
+                        : B->cnt;
     const int group_mod = E ? ctx->n_local : 0;
-    const size_t act_rows = E ? E->r_cap + (size_t)B->t_max : (size_t)B->t_max * 9;
+    const uint16_t *xrows = E ? reinterpret_cast<const uint16_t *>(E->arena + E->L.xr) +
+                                    (size_t)ea.set * E->world * E->C * kHidden
+                              : B->xp;
+    const size_t act_rows = E ? (size_t)E->world * E->C + (size_t)B->t_max : (size_t)B->t_max * 9;
 
     // 4. gate/up + SwiGLU: routed positions and the shared expert
     {
@@ -786,7 +1008,9 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
         r.n_groups = n_groups;
         r.cnt = gcnt;
         r.group_mod = group_mod;
-        r.b_hi = E ? E->xr : B->xp;
+        r.slab_groups = E ? ctx->n_local : 0;
+        r.slab_rows = E ? (int)E->C : 0;
+        r.b_hi = xrows;
         r.passes = kPassHiHi;
         r.epi = kEpiSwiGLU;
         r.ld_out = kInter;
@@ -822,7 +1046,7 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
             ok = ok && make_matrix_maps(B, s, 0, sp, sfmt, kHidden, ps, 32, 16 * ps, 1, 512 * ps, 0, 0, ps);
             ok = ok && make_matrix_maps(B, s, 1, sp + DA.srow, sfmt, kHidden, ps, 32, 16 * ps, 1, 512 * ps, 0, 0, ps);
         }
-        ok = ok && make_bmaps(B, r, E ? (int)E->r_cap : kMaxK * B->t_max) && make_bmaps(B, s, B->t_max);
+        ok = ok && make_bmaps(B, r, E ? (int)(E->world * E->C) : kMaxK * B->t_max) && make_bmaps(B, s, B->t_max);
         if (!ok) {
             nmoe_ctx_set_error(ctx, "gate/up tensor maps");
             return NMOE_ECUDA;
@@ -851,6 +1075,8 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
         r.n_groups = n_groups;
         r.cnt = gcnt;
         r.group_mod = group_mod;
+        r.slab_groups = E ? ctx->n_local : 0;
+        r.slab_rows = E ? (int)E->C : 0;
         r.b_hi = B->act;
         r.passes = kPassHiHi;
         r.epi = kEpiBf16;
@@ -886,24 +1112,24 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
         }
     }
 
-    // 5b. expert parallelism: return the down outputs to the ranks that own the tokens
+    // 5b. expert parallelism: down outputs back to their sources (peer stores), then wait
+    // for every owner's returns
+    const uint16_t *ysrc = B->y;
     if (E != nullptr) {
-        ncclResult_t nr = ncclGroupStart();
-        for (int p = 0; p < E->world && nr == ncclSuccess; ++p) {
-            if (rcnt_s[p]) nr = ncclSend(E->yr + roff[p] * kHidden, (size_t)rcnt_s[p] * kHidden * 2, ncclChar, p, E->comm, st);
-            if (nr == ncclSuccess && scnt[p])
-                nr = ncclRecv(B->y + soff[p] * kHidden, (size_t)scnt[p] * kHidden * 2, ncclChar, p, E->comm, st);
-        }
-        if (nr == ncclSuccess) nr = ncclGroupEnd();
-        if (nr != ncclSuccess) {
-            nmoe_ctx_set_error(ctx, "combine exchange: %s", ncclGetErrorString(nr));
-            return NMOE_ENCCL;
+        if (E->timing) cudaEventRecord(E->ev[2], st);
+        k_ep_return<<<2 * ctx->num_sms, 256, 0, st>>>(ea, E->yr);
+        k_ep_wait<<<1, 32, 0, st>>>(ea, 1, ctx->d_err, B->timeout_ns);
+        if (E->timing) cudaEventRecord(E->ev[3], st);
+        if ((e = cudaGetLastError()) != cudaSuccess) {
+            nmoe_ctx_set_error(ctx, "combine exchange: %s", cudaGetErrorString(e));
+            return NMOE_ECUDA;
         }
         if (T == 0) return NMOE_OK;
+        ysrc = reinterpret_cast<const uint16_t *>(E->arena + E->L.yret) + (size_t)ea.set * E->C * kHidden;
     }
 
     // 6. combine
-    k_combine<<<(T * 256 + 255) / 256, 256, 0, st>>>(B->y, B->w, B->inv, B->score, h_mid, B->p_sdown, nsplit_d, T, k,
+    k_combine<<<(T * 256 + 255) / 256, 256, 0, st>>>(ysrc, B->w, B->inv, B->score, h_mid, B->p_sdown, nsplit_d, T, k,
                                                      out, out_dtype == NMOE_DTYPE_BF16);
     if ((e = cudaGetLastError()) != cudaSuccess) {
         nmoe_ctx_set_error(ctx, "batched launch: %s", cudaGetErrorString(e));
@@ -934,6 +1160,19 @@ extern "C" int nmoe_moe_debug_gemm_trace(nmoe_moe_ctx *ctx, uint32_t *out, int n
     }
     Guard guard(ctx->device);
     if (cudaMemcpy(out, ctx->batched->trace, (size_t)n * 4, cudaMemcpyDeviceToHost) != cudaSuccess) return NMOE_ECUDA;
+    return NMOE_OK;
+}
+
+extern "C" int nmoe_moe_debug_ep_times(nmoe_moe_ctx *ctx, float *ms) {
+    if (ctx == nullptr || ms == nullptr || ctx->ep == nullptr || !ctx->ep->timing) {
+        if (ctx) nmoe_ctx_set_error(ctx, "debug_ep_times: needs world_size > 1 and NMOE_EP_TIMING=1 at create");
+        return NMOE_EINVAL;
+    }
+    Guard guard(ctx->device);
+    EpState *E = ctx->ep;
+    if (cudaEventSynchronize(E->ev[3]) != cudaSuccess) return NMOE_ECUDA;
+    if (cudaEventElapsedTime(&ms[0], E->ev[0], E->ev[1]) != cudaSuccess) return NMOE_ECUDA;
+    if (cudaEventElapsedTime(&ms[1], E->ev[2], E->ev[3]) != cudaSuccess) return NMOE_ECUDA;
     return NMOE_OK;
 }
 

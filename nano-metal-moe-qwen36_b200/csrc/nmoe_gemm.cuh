@@ -76,6 +76,9 @@ struct alignas(64) GemmProblem {
     const int *cnt;           // [n_groups] tokens per group
     int group_mod;            // weight group of group g = g % group_mod (0: g); expert
                               // parallelism orders groups (source rank, local expert)
+    int slab_groups;          // expert parallelism: groups come in slabs of slab_groups (one
+    int slab_rows;            // per source rank) whose rows start at slab * slab_rows (0: the
+                              // groups' rows are contiguous)
     int in_base;              // B row of position p = in_base + p
     int out_base;             // output row = out_base + position (+ split * split_rows)
     int split_rows;
@@ -286,6 +289,12 @@ __device__ __forceinline__ void gemm_build_tables(const GemmParams &P, GemmTable
             if (lane >= o) { xc += a; xi += b; }
         }
         int pc = xc - sc, pi = xi - si;
+        if (pr.slab_groups > 0) {
+            // rows of slab r (groups [r*G, (r+1)*G), lanes [r*G/8, (r+1)*G/8)) start at r*slab_rows
+            const int lanes = pr.slab_groups / 8, r = lane / lanes;
+            const int base = __shfl_sync(0xffffffffu, pc, r * lanes);
+            pc = pc - base + r * pr.slab_rows;
+        }
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             T->goff[prob][8 * lane + j] = pc;

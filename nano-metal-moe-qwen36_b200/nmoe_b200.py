@@ -30,7 +30,7 @@ ABI_SYMBOLS = (
     "nmoe_moe_forward", "nmoe_moe_route", "nmoe_moe_forward_batched", "nmoe_moe_device_status",
     "nmoe_moe_forward_static", "nmoe_moe_static_error", "nmoe_moe_debug_trail", "nmoe_moe_debug_timeline",
     "nmoe_moe_debug_logits", "nmoe_moe_debug_gemm_trace", "nmoe_moe_nccl_unique_id", "nmoe_moe_decode_grid",
-    "nmoe_moe_static_scratch_bytes", "nmoe_moe_static_status",
+    "nmoe_moe_static_scratch_bytes", "nmoe_moe_static_status", "nmoe_moe_debug_ep_times",
 )
 
 
@@ -116,6 +116,8 @@ def lib() -> C.CDLL:
     L.nmoe_moe_debug_timeline.argtypes = [vp, vp, i]
     L.nmoe_moe_decode_grid.restype = i
     L.nmoe_moe_decode_grid.argtypes = [vp]
+    L.nmoe_moe_debug_ep_times.restype = i
+    L.nmoe_moe_debug_ep_times.argtypes = [vp, vp]
     L.nmoe_moe_debug_logits.restype = i
     L.nmoe_moe_debug_logits.argtypes = [vp, vp, i]
     L.nmoe_moe_nccl_unique_id.restype = i
@@ -287,6 +289,13 @@ class Context:
         out = np.zeros((T, 256), np.float32)
         self._check(self._L.nmoe_moe_debug_logits(self.h, out.ctypes.data, T))
         return out
+
+    def debug_ep_times(self):
+        """(dispatch + wait, return + wait) device ms of the last expert-parallel call
+        (context created with NMOE_EP_TIMING=1)."""
+        ms = np.zeros(2, np.float32)
+        self._check(self._L.nmoe_moe_debug_ep_times(self.h, ms.ctypes.data))
+        return float(ms[0]), float(ms[1])
 
     def debug_gemm_trace(self):
         """[13][1024] %clock stamps of CTA 0 of the traced grouped-GEMM launch."""

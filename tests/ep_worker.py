@@ -36,6 +36,15 @@ def main():
         time.sleep(0.05)
     uid = open(idfile, "rb").read()
     torch.cuda.set_device(rank)
+    if len(sys.argv) > 5 and sys.argv[5] == "mismatch":
+        # rank 1 asks for a different t_max: every rank must refuse the context
+        try:
+            N.Context(quant_bits=4, num_layers=1, t_max=64 if rank == 0 else 32, device=rank, world_size=world,
+                      rank=rank, nccl_unique_id=uid)
+        except N.NmoeError as ex:
+            assert ex.status == N.EINVAL and "t_max" in str(ex), ex
+            return
+        raise SystemExit("a context with mismatched t_max was created")
     ctx = N.Context(quant_bits=4, num_layers=1, t_max=64, device=rank, world_size=world, rank=rank,
                     nccl_unique_id=uid)
     lw = O.make_layer(300, bits=4, distinct_experts=24)

@@ -1,14 +1,17 @@
 """Expert-parallel dispatch and combine on two CPU ranks (gloo), against the
 single-process routed sum.
 
-This mirrors the plan nmoe_moe_forward_batched follows when world_size > 1: every rank
-routes its own tokens over all 256 experts; (token, slot) rows are ordered by global
-expert, so each destination rank's rows form one contiguous segment; ranks exchange the
-per-expert counts, then the rows; each rank applies its own experts (32 per rank at 8
-GPUs, 128 here) to the rows it received, in (source rank, local expert) order; the
-outputs go back to their source ranks in the order they were sent, and the source
-combines sum_s w_s * down_s. Gate/up/down use the oracle's expert functions, so the EP
-result must equal the local one exactly."""
+This mirrors the plan nmoe_moe_forward_batched follows when world_size > 1 (the device
+does it with NVLink peer stores; here fixed-size gloo messages stand in for them): every
+rank routes its own tokens over all 256 experts; (token, slot) rows are ordered by global
+expert, so each destination rank's rows form one contiguous segment; each rank writes its
+segment into slab `rank` (fixed capacity C = T_max * K rows, so no sizes are exchanged
+first) of the destination's receive buffer, together with its per-expert counts and the
+segment's first position; the destination applies its own experts (128 per rank here, 32
+at 8 GPUs) to every slab in (source rank, local expert) order and writes each output back
+into the source's return buffer at the position the row left from; the source combines
+sum_s w_s * down_s. Gate/up/down use the oracle's expert functions, so the EP result must
+equal the local one exactly. Rank 1 has fewer tokens than rank 0."""
 import os
 import socket
 
@@ -20,7 +23,9 @@ import torch.multiprocessing as mp
 
 from oracle import oracle as O
 
-W, T, K, E = 2, 6, 4, 256
+W, K, E = 2, 4, 256
+T_RANK = (6, 3)
+C = max(T_RANK) * K   # slab capacity: every token could send all K rows to one rank
 
 
 def _free_port():
@@ -46,10 +51,10 @@ def _worker(rank, port, q):
         os.environ["MASTER_ADDR"] = "127.0.0.1"
         os.environ["MASTER_PORT"] = str(port)
         dist.init_process_group("gloo", rank=rank, world_size=W)
+        T = T_RANK[rank]
         lw = O.make_layer(11, bits=4, distinct_experts=6)
         x = np.random.default_rng(100 + rank).standard_normal((T, 2048), dtype=np.float32)
         nl = E // W
-        # route (oracle logits) and order (token, slot) rows by global expert, then token
         idx, w = np.zeros((T, K), np.int64), np.zeros((T, K), np.float32)
         for t in range(T):
             r = O.block_forward(lw, K, x[t])
@@ -57,63 +62,56 @@ def _worker(rank, port, q):
         rows = sorted(((int(idx[t, s]), t, s) for t in range(T) for s in range(K)))
         pos = {(t, s): p for p, (_, t, s) in enumerate(rows)}
         cnt = np.bincount([e for e, _, _ in rows], minlength=E).astype(np.int64)
-        # exchange counts: rank p gets cnt[p*nl:(p+1)*nl] from every source
-        rcnt = [torch.zeros(nl, dtype=torch.int64) for _ in range(W)]
+        off = np.concatenate([[0], np.cumsum(cnt)])          # first position of each expert's rows
+
+        def exchange(msgs):   # one fixed-size message to every rank (self included)
+            got = [None] * W
+            reqs = []
+            for p in range(W):
+                if p == rank:
+                    got[p] = msgs[p].clone()
+                else:
+                    got[p] = torch.zeros_like(msgs[p])
+                    reqs.append(dist.isend(msgs[p], p))
+                    reqs.append(dist.irecv(got[p], p))
+            for r_ in reqs:
+                r_.wait()
+            return got
+
+        # dispatch: slab for destination p = rows of experts [p*nl, (p+1)*nl), then counts, offset
+        msgs = []
         for p in range(W):
-            if p == rank:
-                rcnt[p] = torch.from_numpy(cnt[p * nl:(p + 1) * nl].copy())
-        reqs = []
-        for p in range(W):
-            if p != rank:
-                reqs.append(dist.isend(torch.from_numpy(cnt[p * nl:(p + 1) * nl].copy()), p))
-                reqs.append(dist.irecv(rcnt[p], p))
-        for r_ in reqs:
-            r_.wait()
-        scnt = [int(cnt[p * nl:(p + 1) * nl].sum()) for p in range(W)]
-        soff = np.concatenate([[0], np.cumsum(scnt)])
-        send = np.stack([x[t] for _, t, _ in rows])
-        recv = [None] * W
-        reqs = []
-        for p in range(W):
-            n_in = int(rcnt[p].sum())
-            recv[p] = torch.zeros((n_in, 2048), dtype=torch.float32)
-            if p == rank:
-                recv[p] = torch.from_numpy(send[soff[p]:soff[p + 1]].copy())
-            else:
-                reqs.append(dist.isend(torch.from_numpy(send[soff[p]:soff[p + 1]].copy()), p))
-                reqs.append(dist.irecv(recv[p], p))
-        for r_ in reqs:
-            r_.wait()
-        # apply this rank's experts in (source, local expert) order
+            slab = np.zeros((C, 2048), np.float32)
+            for e, t, s in rows:
+                if e // nl == p:
+                    slab[pos[(t, s)] - off[p * nl]] = x[t]
+            meta = np.concatenate([cnt[p * nl:(p + 1) * nl], [off[p * nl]]]).astype(np.float32)
+            msgs.append(torch.from_numpy(np.concatenate([slab.ravel(), meta])))
+        recv = exchange(msgs)
+        # this rank's experts over every source's slab, in (source, local expert) order;
+        # outputs written into a return message at the source's positions
         back = []
-        for p in range(W):
-            y = np.zeros((recv[p].shape[0], 2048), np.float32)
+        for r in range(W):
+            m = recv[r].numpy()
+            slab = m[: C * 2048].reshape(C, 2048)
+            rc = m[C * 2048: C * 2048 + nl].astype(np.int64)
+            first = int(m[-1])
+            ret = np.zeros((C, 2048), np.float32)
             i = 0
             for j in range(nl):
-                for _ in range(int(rcnt[p][j])):
-                    y[i] = _expert(lw, rank * nl + j, recv[p][i].numpy())
+                for _ in range(int(rc[j])):
+                    ret[first + i] = _expert(lw, rank * nl + j, slab[i])
                     i += 1
-            back.append(torch.from_numpy(y))
-        # return outputs; they arrive in send order
-        ret = [None] * W
-        reqs = []
-        for p in range(W):
-            ret[p] = torch.zeros((scnt[p], 2048), dtype=torch.float32)
-            if p == rank:
-                ret[p] = back[p]
-            else:
-                reqs.append(dist.isend(back[p], p))
-                reqs.append(dist.irecv(ret[p], p))
-        for r_ in reqs:
-            r_.wait()
-        yall = torch.cat(ret).numpy()
+            back.append(torch.from_numpy(ret.ravel()))
+        rets = exchange(back)
+        yret = sum(r.numpy().reshape(C, 2048) for r in rets)   # owners write disjoint positions
         ep = np.zeros((T, 2048), np.float32)
         local = np.zeros((T, 2048), np.float32)
         for t in range(T):
             for s in range(K):
-                ep[t] += w[t, s] * yall[pos[(t, s)]]
+                ep[t] += w[t, s] * yret[pos[(t, s)]]
                 local[t] += w[t, s] * _expert(lw, int(idx[t, s]), x[t])
-        q.put((rank, float(np.abs(ep - local).max()), sorted(set(scnt))))
+        q.put((rank, float(np.abs(ep - local).max()) if T else 0.0, int(cnt.sum())))
         dist.destroy_process_group()
     except Exception as ex:  # surface worker failures to the test
         q.put((rank, repr(ex), None))

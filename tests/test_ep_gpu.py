@@ -1,5 +1,6 @@
-"""Expert-parallel forward_batched on 2 GPUs (one process per GPU, NCCL exchange of
-token rows), against the single-GPU path on the same tokens. Needs >= 2 GPUs."""
+"""Expert-parallel forward_batched on 2 GPUs (one process per GPU, token rows exchanged by
+NVLink peer stores), against the single-GPU path on the same tokens; and the collective
+refusal of ranks whose t_max differ. Needs >= 2 GPUs."""
 import os
 import subprocess
 import sys
@@ -52,3 +53,20 @@ def test_ep_two_gpus_matches_single_gpu(tmp_path, counts):
             np.testing.assert_array_equal(np.load(tmp_path / f"idx{r}_{call}.npy"), idx.cpu().numpy())
             got = np.load(tmp_path / f"out{r}_{call}.npy")
             assert rel_l2(got, out.cpu().numpy()) < 1e-3, (r, call)
+
+
+def test_ep_mismatched_t_max_is_refused(tmp_path):
+    """The receive slabs have one capacity on every rank: ranks created with different
+    t_max all fail with NMOE_EINVAL instead of one of them overrunning another's slab."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    procs = [subprocess.Popen([sys.executable, os.path.join(HERE, "ep_worker.py"), str(r), "2", "8", str(tmp_path),
+                               "mismatch"], env=env) for r in range(2)]
+    try:
+        rcs = [p.wait(timeout=300) for p in procs]
+    finally:
+        for p in procs:
+            if p.poll() is None:
+                p.kill()
+    assert rcs == [0, 0]
