@@ -667,7 +667,77 @@ def run_ours(args, rank, world, local_rank):
         if calib is not None:
             result["config"]["router_skew"] = calib
     ctx.close()
+    del outs, xs
+    torch.cuda.empty_cache()
+    if args.ep_tokens > 0:
+        ep = run_ep_batched(args, rank, world, dev)
+        if result is not None:
+            result["ep_batched"] = ep
     return result
+
+
+def run_ep_batched(args, rank, world, dev):
+    """Config 2 beside the decode line, at every N: T tokens per rank (--ep-tokens) through
+    --ep-layers resident layers per step, experts sharded 256/N per GPU with token rows
+    exchanged over NVLink (one GPU: the plain batched path). Device-timed, max over ranks;
+    with N > 1 also the device time of the two exchanges of one call."""
+    import torch
+    import torch.distributed as dist
+    import nmoe_b200 as N
+    T, L = args.ep_tokens, args.ep_layers
+    layers, _, _ = build_workload(L, 4, 8, N.DTYPE_BF16, N.DTYPE_BF16, pool=args.pool, seed=args.seed)
+    uid = None
+    if world > 1:
+        obj = [N.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        uid = obj[0]
+        os.environ["NMOE_EP_TIMING"] = "1"
+    ctx = N.Context(quant_bits=4, num_layers=L, t_max=T, device=dev, world_size=world, rank=rank, nccl_unique_id=uid)
+    for l, lw in enumerate(layers):
+        ctx.load_layer(l, lw.experts)
+        ctx.set_dense(l, lw.router, lw.shared_gate, lw.shared_up, lw.shared_down, lw.shared_gate_vec)
+    del layers
+    from oracle import oracle as O
+    xh = O.f32_to_bf16(np.random.default_rng(args.seed + 1000 + rank).standard_normal((T, HIDDEN), dtype=np.float32))
+    x = torch.from_numpy(xh.view(np.int16)).to(f"cuda:{dev}")
+    out = torch.zeros((T, HIDDEN), dtype=torch.float32, device=f"cuda:{dev}")
+    stream = torch.cuda.Stream(device=dev)
+
+    def step():
+        for l in range(L):
+            ctx.forward_batched(l, T, 8, x, out, stream=stream.cuda_stream)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    steps = max(5, args.steps // 2)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=f"cuda:{dev}")
+    exch = None
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        d, r = ctx.debug_ep_times()
+        ex = torch.tensor([d, r], dtype=torch.float64, device=f"cuda:{dev}")
+        dist.all_reduce(ex, op=dist.ReduceOp.MAX)
+        exch = {"dispatch_and_wait_ms": float(ex[0]), "return_and_wait_ms": float(ex[1]),
+                "transport": "NVLink peer stores into IPC-mapped slabs (no NCCL on the call path)"}
+    rc, code = ctx.device_status()
+    ctx.close()
+    if rc != N.OK:
+        raise RuntimeError(f"expert-parallel device error word {code}")
+    per_call_ms = float(ms.item()) / (steps * L)
+    return {"metric": "routed-MoE tokens/s/layer (batched, config 2)", "value": world * T / (per_call_ms / 1e3),
+            "unit": "tokens/s/layer", "per_rank_value": T / (per_call_ms / 1e3), "per_call_ms": per_call_ms,
+            "tokens_per_rank": T, "layers": L, "ranks": world, "scaling": "weak",
+            "parallelism": f"expert parallel, {EXPERTS // world} experts per GPU" if world > 1 else "single GPU",
+            "exchange": exch, "timing": "CUDA events around the step loop, max over ranks"}
 
 
 _JSON_OUT = sys.stdout
@@ -688,6 +758,9 @@ def main():
     ap.add_argument("--k", type=int, default=8, help="decode: routed experts per token (config 1 sweeps 1..8)")
     ap.add_argument("--tokens", type=int, default=4096, help="T for --workload batched")
     ap.add_argument("--batched-layers", type=int, default=4, help="resident layers cycled by --workload batched")
+    ap.add_argument("--ep-tokens", type=int, default=4096,
+                    help="decode workload: also time config 2 at this many tokens per rank (0: skip)")
+    ap.add_argument("--ep-layers", type=int, default=2)
     ap.add_argument("--prefetch", action="store_true",
                     help="let each layer call prefetch the next layer's router/shared weights to L2")
     args = ap.parse_args()

@@ -47,6 +47,7 @@ struct BatchedState {
     int *rank = nullptr, *inv = nullptr;     // [t_max][8]
     int *perm = nullptr;                     // [t_max * 8]
     int *cnt = nullptr;                      // [256]
+    int *eoff = nullptr;                     // [256] first position of each expert's rows
     uint16_t *act = nullptr;                 // [t_max * 9][512]  (routed positions, then shared)
     uint16_t *y = nullptr;                   // [t_max * 8][2048] routed down outputs
     int rows_cap = 0;                        // rows of each partial-sum buffer
@@ -235,7 +236,7 @@ __global__ void __launch_bounds__(kRouteWarps * 32) k_route(const RouteArgs a) {
 
 // Position of (t, s) = exclusive prefix of counts over the experts before e + rank.
 __global__ void k_scatter(const uint32_t *idx, const int *rank, const int *cnt, int T, int k, int expert_lo,
-                          int n_local, int *perm, int *inv) {
+                          int n_local, int *perm, int *inv, int *eoff) {
     __shared__ int off[kExperts];
     __shared__ int wsum[8];
     const int tid = threadIdx.x;   // 256 threads
@@ -252,6 +253,7 @@ __global__ void k_scatter(const uint32_t *idx, const int *rank, const int *cnt, 
     int base = 0;
     for (int i = 0; i < warp; ++i) base += wsum[i];
     off[tid] = base + x - c;
+    if (blockIdx.x == 0 && eoff) eoff[tid] = off[tid];   // first position of each expert's rows
     __syncthreads();
     const int i = blockIdx.x * blockDim.x + tid;
     if (i >= T * k) return;
@@ -359,24 +361,6 @@ __global__ void k_combine(const uint16_t *y, const float *w, const int *inv, con
 
 // ------------------------------------------------------ expert parallelism ----
 
-// Exclusive prefix over the 256 per-expert counts (256 threads): off[e] = sum_{e' < e} cnt[e'].
-__device__ __forceinline__ void block_prefix256(const int *cnt, int *off, int *wsum) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int c = cnt[tid];
-    int x = c;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, x, o);
-        if (lane >= o) x += y;
-    }
-    if (lane == 31) wsum[warp] = x;
-    __syncthreads();
-    int base = 0;
-    for (int i = 0; i < warp; ++i) base += wsum[i];
-    off[tid] = base + x - c;
-    __syncthreads();
-}
-
 __device__ __forceinline__ void st_release_sys_u32(uint32_t *p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -411,29 +395,27 @@ __device__ __forceinline__ void ep_signal_last(const EpArgs &a, int which, unsig
     }
 }
 
-// Dispatch: block b < T*k copies row (t, s) = (b / k, b % k) of xh into slab `rank` of the
-// owner of its expert; blocks b < world also write that destination's counts and this
-// rank's segment offset. Grid: max(T*k, world) blocks of 256 threads.
+// Dispatch: rows (t, s) of xh (grid-stride, one row per block iteration) go into slab
+// `rank` of the owner of their expert, at (position - first position of that owner's
+// experts, eoff); blocks b < world also write that destination's counts and this rank's
+// segment offset. Grid: at least `world` blocks of 256 threads.
 __global__ void __launch_bounds__(256) k_ep_dispatch(EpArgs a, const uint16_t *xh, const uint32_t *idx,
-                                                     const int *inv, const int *cnt, int T, int k) {
-    __shared__ int off[kExperts];
-    __shared__ int wsum[8];
-    block_prefix256(cnt, off, wsum);
-    const int b = blockIdx.x, tid = threadIdx.x, nl = a.n_local;
-    if (b < T * k) {
-        const int t = b / k, s = b - t * k;
+                                                     const int *inv, const int *cnt, const int *eoff, int T, int k) {
+    const int tid = threadIdx.x, nl = a.n_local;
+    for (int q = blockIdx.x; q < T * k; q += gridDim.x) {
+        const int t = q / k, s = q - t * k;
         const int pos = inv[(size_t)t * kMaxK + s];
-        if (pos >= 0) {
-            const int p = (int)idx[(size_t)t * kMaxK + s] / nl;
-            const size_t row = ((size_t)a.set * a.world + a.rank) * a.C + (size_t)(pos - off[p * nl]);
-            uint4 *dst = reinterpret_cast<uint4 *>(a.peer[p] + a.L.xr) + row * (kHidden / 8);
-            dst[tid] = reinterpret_cast<const uint4 *>(xh + (size_t)t * kHidden)[tid];
-        }
+        if (pos < 0) continue;
+        const int p = (int)idx[(size_t)t * kMaxK + s] / nl;
+        const size_t row = ((size_t)a.set * a.world + a.rank) * a.C + (size_t)(pos - eoff[p * nl]);
+        uint4 *dst = reinterpret_cast<uint4 *>(a.peer[p] + a.L.xr) + row * (kHidden / 8);
+        dst[tid] = reinterpret_cast<const uint4 *>(xh + (size_t)t * kHidden)[tid];
     }
+    const int b = blockIdx.x;
     if (b < a.world) {
         int *rc = reinterpret_cast<int *>(a.peer[b] + a.L.rcnt) + ((size_t)a.set * a.world + a.rank) * nl;
         if (tid < nl) rc[tid] = cnt[b * nl + tid];
-        if (tid == 0) reinterpret_cast<int *>(a.peer[b] + a.L.rmeta)[a.set * a.world + a.rank] = off[b * nl];
+        if (tid == 0) reinterpret_cast<int *>(a.peer[b] + a.L.rmeta)[a.set * a.world + a.rank] = eoff[b * nl];
     }
     ep_signal_last(a, 0, a.done);
 }
@@ -788,6 +770,7 @@ int nmoe_batched_init(nmoe_moe_ctx *ctx) {
         {(void **)&B->w, T * kMaxK * 4},          {(void **)&B->idx, T * kMaxK * 4},
         {(void **)&B->rank, T * kMaxK * 4},       {(void **)&B->inv, T * kMaxK * 4},
         {(void **)&B->perm, T * kMaxK * 4},       {(void **)&B->cnt, kExperts * 4},
+        {(void **)&B->eoff, kExperts * 4},
         {(void **)&B->act, act_rows * kInter * 2}, {(void **)&B->y, T * 8 * kHidden * 2},
         {(void **)&B->p_router, R * kExperts * 4}, {(void **)&B->p_sgu, R * 2 * kInter * 4},
         {(void **)&B->p_sdown, R * kHidden * 4},
@@ -807,7 +790,7 @@ void nmoe_batched_destroy(nmoe_moe_ctx *ctx) {
     BatchedState *B = ctx->batched;
     if (B == nullptr) return;
     void *ps[] = {B->xh,   B->xl,  B->xp,  B->logits, B->score, B->w,        B->idx,  B->rank,
-                  B->inv,  B->perm, B->cnt,   B->act,   B->y,        B->p_router, B->p_sgu, B->p_sdown,
+                  B->inv,  B->perm, B->cnt, B->eoff,   B->act,   B->y,        B->p_router, B->p_sgu, B->p_sdown,
                   B->trace};
     for (void *p : ps)
         if (p) cudaFree(p);
@@ -955,7 +938,7 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
         if (T > 0) {
             k_route<<<(T + kRouteWarps - 1) / kRouteWarps, kRouteWarps * 32, 0, st>>>(a);
             k_scatter<<<(T * k + 255) / 256, 256, 0, st>>>(B->idx, B->rank, B->cnt, T, k, a.expert_lo, a.n_local,
-                                                           B->perm, B->inv);
+                                                           B->perm, B->inv, B->eoff);
             if (E == nullptr) k_gather_rows<<<T * k, 256, 0, st>>>(B->xh, B->perm, T, k, B->xp);
         }
     }
@@ -976,7 +959,9 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
         ea.done = E->done;
         ++E->call;
         if (E->timing) cudaEventRecord(E->ev[0], st);
-        k_ep_dispatch<<<std::max(T * k, E->world), 256, 0, st>>>(ea, B->xh, B->idx, B->inv, B->cnt, T, k);
+        if (T == 0) cudaMemsetAsync(B->eoff, 0, kExperts * sizeof(int), st);
+        k_ep_dispatch<<<std::max(std::min(T * k, 16 * ctx->num_sms), E->world), 256, 0, st>>>(ea, B->xh, B->idx, B->inv,
+                                                                                          B->cnt, B->eoff, T, k);
         k_ep_wait<<<1, 32, 0, st>>>(ea, 0, ctx->d_err, B->timeout_ns);
         if (E->timing) cudaEventRecord(E->ev[1], st);
         if ((e = cudaGetLastError()) != cudaSuccess) {
@@ -1117,7 +1102,7 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
     const uint16_t *ysrc = B->y;
     if (E != nullptr) {
         if (E->timing) cudaEventRecord(E->ev[2], st);
-        k_ep_return<<<2 * ctx->num_sms, 256, 0, st>>>(ea, E->yr);
+        k_ep_return<<<16 * ctx->num_sms, 256, 0, st>>>(ea, E->yr);
         k_ep_wait<<<1, 32, 0, st>>>(ea, 1, ctx->d_err, B->timeout_ns);
         if (E->timing) cudaEventRecord(E->ev[3], st);
         if ((e = cudaGetLastError()) != cudaSuccess) {
