@@ -11,6 +11,7 @@ plus router and shared expert (21.5 MB), so a step touches ~860 MB, far above th
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
   python bench.py --workload batched --tokens T     (T tokens a call)
+  python bench.py --workload lm_head [--lm-dtypes q4,bf16]   (LM head alone)
 
 ours: `value` = layer calls / s with inputs resident in HBM (CUDA graph of the 40
 calls, timed with CUDA events, max over ranks); `e2e` = the same metric through the C
@@ -669,11 +670,95 @@ def run_ours(args, rank, world, local_rank):
     ctx.close()
     del outs, xs
     torch.cuda.empty_cache()
+    if args.lm_head and rank == 0:
+        result["lm_head"] = run_lm_head(args, dev)
     if args.ep_tokens > 0:
         ep = run_ep_batched(args, rank, world, dev)
         if result is not None:
             result["ep_batched"] = ep
     return result
+
+
+LM_VOCAB = 248320   # src/runtime.m:1911
+
+
+def lm_head_bytes(dtype: int, vocab: int = LM_VOCAB) -> int:
+    """Algorithmic bytes of one token-only LM head call: every weight byte once, plus x and
+    the RMSNorm weight (the token is 4 bytes)."""
+    per_row = HIDDEN // 2 + 2 * (HIDDEN // 64) * 2 if dtype == 4 else HIDDEN * 2
+    return vocab * per_row + HIDDEN * 4 + HIDDEN * 2
+
+
+def run_lm_head(args, dev):
+    """The LM head (final RMSNorm + 248,320-row GEMV + top-1, one launch) at the reference's
+    vocab, q4 (the reference's lm_head) and bf16: device time per call (CUDA graph of calls,
+    each reading 0.29 / 1.02 GB, above L2), roofline against measured HBM, the oracle's time
+    for one call on the host cores, and a parity check of one call against the oracle."""
+    import torch
+    import nmoe_b200 as N
+    from oracle import oracle as O
+    out = {}
+    rng = np.random.default_rng(args.seed + 77)
+    xh = rng.standard_normal(HIDDEN).astype(np.float32)
+    nw = O.f32_to_bf16(rng.standard_normal(HIDDEN).astype(np.float32) * 0.1)
+    pk, pk_kind = peaks()
+    stream = torch.cuda.Stream(device=dev)
+    want = [t.strip() for t in args.lm_dtypes.split(",")]
+    for dt, name in ((N.DTYPE_Q4, "q4"), (N.DTYPE_BF16, "bf16")):
+        if name not in want:
+            continue
+        head = O.make_lm_head(args.seed + 5, LM_VOCAB, dt)
+        d = {"weight": torch.from_numpy(head.weight.view(np.int32) if dt == N.DTYPE_Q4 else head.weight.view(np.int16))
+             .to(f"cuda:{dev}")}
+        if dt == N.DTYPE_Q4:
+            d["scales"] = torch.from_numpy(head.scales.view(np.int16)).to(f"cuda:{dev}")
+            d["biases"] = torch.from_numpy(head.biases.view(np.int16)).to(f"cuda:{dev}")
+        x = torch.from_numpy(xh).to(f"cuda:{dev}")
+        nwd = torch.from_numpy(nw.view(np.int16)).to(f"cuda:{dev}")
+        tok = torch.zeros(1, dtype=torch.int32, device=f"cuda:{dev}")
+        ws = torch.zeros(N.lm_head_workspace_bytes() // 8, dtype=torch.int64, device=f"cuda:{dev}")
+        lg = torch.empty(LM_VOCAB, dtype=torch.float32, device=f"cuda:{dev}")
+        # parity of one call (logits requested) against the oracle
+        N.lm_head_argmax(d, dt, LM_VOCAB, x, tok, ws, norm_weight=nwd, logits_out=lg, stream=stream.cuda_stream)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        otok, ol = O.lm_head_argmax(head, xh, nw)
+        cpu_s = time.perf_counter() - t0
+        glg = lg.cpu().numpy()
+        err = float(np.abs(glg - ol).max() / np.abs(ol).max())
+        gtok = int(tok.item())
+        if err > 3e-6 or gtok != O.argmax_top1(glg):
+            raise RuntimeError(f"lm head {name} disagrees with the oracle: rel err {err}, token {gtok} vs {otok}")
+        reps = 20
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for _ in range(reps):
+                N.lm_head_argmax(d, dt, LM_VOCAB, x, tok, ws, norm_weight=nwd,
+                                 stream=torch.cuda.current_stream().cuda_stream)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_rep = 10
+        e0.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(n_rep):
+                g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (n_rep * reps)
+        ab = lm_head_bytes(dt)
+        ach = ab / (us * 1e-6) / 1e9
+        out[name] = {"us_per_call": us, "calls_per_s": 1e6 / us, "token": gtok, "oracle_token": otok,
+                     "logits_max_rel_err": err,
+                     "roofline": {"bound": "hbm", "achieved": ach, "peak": pk, "unit": "GB/s", "frac": ach / pk,
+                                  "peak_kind": pk_kind, "algorithmic_bytes_per_launch": ab},
+                     "cpu_oracle_ms_per_call": cpu_s * 1e3, "cpu_oracle_threads": O.lib().orc_get_threads()}
+        del g, d, x, lg, head
+        torch.cuda.empty_cache()
+    out["config"] = {"vocab": LM_VOCAB, "in_dim": HIDDEN, "norm": "model.norm RMSNorm fused (eps 1e-6, w+1)",
+                     "timing": "CUDA graph of 20 token-only calls x 10 replays, CUDA events; weights above L2"}
+    return out
 
 
 def run_ep_batched(args, rank, world, dev):
@@ -753,7 +838,8 @@ def main():
     ap.add_argument("--pool", type=int, default=32, help="distinct expert packs generated on the host")
     ap.add_argument("--seed", type=int, default=2026)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--workload", choices=["decode", "batched"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "batched", "lm_head"], default="decode")
+    ap.add_argument("--lm-dtypes", default="q4,bf16", help="LM head weight types timed (q4, bf16)")
     ap.add_argument("--bits", type=int, choices=[2, 4], default=4, help="decode: expert packs (4: config 0, 2: config 1)")
     ap.add_argument("--k", type=int, default=8, help="decode: routed experts per token (config 1 sweeps 1..8)")
     ap.add_argument("--tokens", type=int, default=4096, help="T for --workload batched")
@@ -761,6 +847,7 @@ def main():
     ap.add_argument("--ep-tokens", type=int, default=4096,
                     help="decode workload: also time config 2 at this many tokens per rank (0: skip)")
     ap.add_argument("--ep-layers", type=int, default=2)
+    ap.add_argument("--lm-head", type=int, default=1, help="also time the LM head (rank 0) beside the decode line")
     ap.add_argument("--prefetch", action="store_true",
                     help="let each layer call prefetch the next layer's router/shared weights to L2")
     args = ap.parse_args()
@@ -784,7 +871,12 @@ def main():
         import torch.distributed as dist
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local_rank}"))
-    res = (run_batched if args.workload == "batched" else run_ours)(args, rank, world, local_rank)
+    if args.workload == "lm_head":
+        import torch
+        torch.cuda.set_device(local_rank)
+        res = {"workload": "lm_head", **run_lm_head(args, local_rank)} if rank == 0 else None
+    else:
+        res = (run_batched if args.workload == "batched" else run_ours)(args, rank, world, local_rank)
     if res is not None:
         print(json.dumps(res), file=_JSON_OUT, flush=True)
     if world > 1:

@@ -249,6 +249,33 @@ size_t nmoe_moe_static_scratch_bytes(void);
  * in *code (may be NULL). Races, like the calls, with static calls that overlap it. */
 int nmoe_moe_static_status(int *code, void *stream);
 
+/* ---- LM head: final RMSNorm + vocab GEMV + top-1 in one launch ------------------
+ * Replaces NMOERunLmHeadArgmaxQ4Metal (src/runtime.m:1882-1948: kernels
+ * nmoe_lm_head_argmax_q4 + nmoe_lm_head_argmax_reduce, metal/kernels.metal:1599-1713)
+ * and the model.norm RMSNorm before it (src/runtime.m:3786, nmoe_rms_norm
+ * metal/kernels.metal:862-900); with logits_out it also covers the fallback
+ * (dequant matvec + nmoe_argmax_top1, src/runtime.m:3793-3794).
+ *   head: DEVICE tensors. q4: weight u32 [vocab][256], scales/biases bf16 [vocab][32]
+ *         (lm_head.weight/.scales/.biases, group 64); bf16: weight [vocab][2048].
+ *         16-byte aligned.
+ *   in_dim: must be 2048. x: DEVICE [2048] f32 or bf16 (x_dtype).
+ *   norm_weight: DEVICE bf16 [2048] (model.norm.weight) or NULL to use x as given;
+ *         x_n = x * rsqrt(mean(x^2) + norm_eps) * (w + (norm_add_one ? 1 : 0)).
+ *   logits_out: DEVICE f32 [vocab] or NULL. token_out: DEVICE u32 [1].
+ *   workspace: DEVICE, nmoe_lm_head_workspace_bytes() bytes, 8-byte aligned, zeroed
+ *         by the caller ONCE; every call leaves it zeroed again. Calls that share a
+ *         workspace must not overlap on the GPU.
+ * Token rule (both reference kernels): lowest row index among the rows with the maximum
+ * logit; NaN, -inf and -FLT_MAX never win; 0 if no row qualifies. A bounded device wait
+ * that expired writes UINT32_MAX as the token (the reference's "no token" value,
+ * src/runtime.m:3804). Asynchronous on `stream`; allocates nothing; capturable.
+ * Message of a failed call: nmoe_lm_head_error(). */
+int nmoe_lm_head_argmax(const nmoe_tensor *head, int head_dtype, int vocab, int in_dim, const void *x,
+                        int x_dtype, const uint16_t *norm_weight, float norm_eps, int norm_add_one,
+                        float *logits_out, uint32_t *token_out, void *workspace, void *stream);
+size_t nmoe_lm_head_workspace_bytes(void);
+const char *nmoe_lm_head_error(void);
+
 #ifdef __cplusplus
 }
 #endif

@@ -31,6 +31,7 @@ ABI_SYMBOLS = (
     "nmoe_moe_forward_static", "nmoe_moe_static_error", "nmoe_moe_debug_trail", "nmoe_moe_debug_timeline",
     "nmoe_moe_debug_logits", "nmoe_moe_debug_gemm_trace", "nmoe_moe_nccl_unique_id", "nmoe_moe_decode_grid",
     "nmoe_moe_static_scratch_bytes", "nmoe_moe_static_status", "nmoe_moe_debug_ep_times",
+    "nmoe_lm_head_argmax", "nmoe_lm_head_workspace_bytes", "nmoe_lm_head_error",
 )
 
 
@@ -124,6 +125,10 @@ def lib() -> C.CDLL:
     L.nmoe_moe_nccl_unique_id.argtypes = [vp, sz]
     L.nmoe_moe_debug_gemm_trace.restype = i
     L.nmoe_moe_debug_gemm_trace.argtypes = [vp, vp, i]
+    L.nmoe_lm_head_argmax.restype = i
+    L.nmoe_lm_head_argmax.argtypes = [C.POINTER(Tensor), i, i, i, vp, i, vp, C.c_float, i, vp, vp, vp, vp]
+    L.nmoe_lm_head_workspace_bytes.restype = sz
+    L.nmoe_lm_head_error.restype = C.c_char_p
     _lib = L
     return L
 
@@ -352,3 +357,21 @@ def static_status(stream=0):
     code = C.c_int(0)
     rc = L.nmoe_moe_static_status(C.byref(code), stream)
     return rc, code.value
+
+
+def lm_head_workspace_bytes() -> int:
+    return int(lib().nmoe_lm_head_workspace_bytes())
+
+
+def lm_head_argmax(head: dict, head_dtype: int, vocab: int, x, token_out, workspace, x_dtype=DTYPE_F32,
+                   norm_weight=None, norm_eps=1e-6, norm_add_one=True, logits_out=None, stream=0):
+    """nmoe_lm_head_argmax: final RMSNorm + LM head GEMV + top-1 in one launch.
+    `head` = {"weight", ["scales", "biases"]} device tensors/pointers; `token_out` a device
+    u32 [1]; `workspace` device memory of lm_head_workspace_bytes(), zeroed once."""
+    t = Tensor(_ptr(head["weight"]), _ptr(head.get("scales")), _ptr(head.get("biases")))
+    L = lib()
+    rc = L.nmoe_lm_head_argmax(C.byref(t), head_dtype, vocab, HIDDEN, _ptr(x), x_dtype, _ptr(norm_weight),
+                               norm_eps, int(bool(norm_add_one)), _ptr(logits_out), _ptr(token_out),
+                               _ptr(workspace), stream)
+    if rc != OK:
+        raise NmoeError(rc, L.nmoe_lm_head_error().decode())

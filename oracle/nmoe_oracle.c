@@ -16,6 +16,7 @@
  */
 #include "nmoe_oracle.h"
 
+#include <float.h>
 #include <math.h>
 #include <stdlib.h>
 #include <string.h>
@@ -450,4 +451,50 @@ int orc_moe_block_forward_batched(const orc_layer *L, int T, int k, const float 
                                     w ? w + (size_t)t * ORC_MAX_K : NULL, NULL, NULL, NULL);
     }
     return rc;
+}
+
+/* ------------------------------------------------------------- LM head ---- */
+
+void orc_rms_norm(const float *x, const uint16_t *w_bf16, float *out, size_t n, float eps, int add_one) {
+    double ss = 0.0;
+    for (size_t i = 0; i < n; i++) ss += (double)x[i] * (double)x[i];
+    const float inv = 1.0f / sqrtf((float)(ss / (double)n) + eps);
+    for (size_t i = 0; i < n; i++) {
+        float w = 1.0f;
+        if (w_bf16 != NULL) {
+            w = orc_bf16_to_f32(w_bf16[i]);
+            if (add_one) w += 1.0f;
+        }
+        out[i] = x[i] * inv * w;
+    }
+}
+
+uint32_t orc_argmax_top1(const float *v, size_t n) {
+    float best = -FLT_MAX;
+    uint32_t idx = 0;
+    for (size_t i = 0; i < n; i++)
+        if (v[i] > best) {   /* strict: the earlier index keeps a tie; NaN compares false */
+            best = v[i];
+            idx = (uint32_t)i;
+        }
+    return idx;
+}
+
+uint32_t orc_lm_head_argmax(int dtype, const void *w, const uint16_t *s, const uint16_t *b, size_t vocab,
+                            size_t in_dim, const float *x, const uint16_t *norm_w, float eps, int add_one,
+                            float *logits) {
+    float *xn = (float *)malloc(in_dim * sizeof(float));
+    float *lg = logits != NULL ? logits : (float *)malloc(vocab * sizeof(float));
+    if (norm_w != NULL)
+        orc_rms_norm(x, norm_w, xn, in_dim, eps, add_one);
+    else
+        memcpy(xn, x, in_dim * sizeof(float));
+    if (dtype == ORC_DTYPE_BF16)
+        orc_bf16_matvec((const uint16_t *)w, xn, lg, vocab, in_dim);
+    else
+        orc_dequant_matvec((const uint32_t *)w, s, b, xn, lg, vocab, in_dim, 4, 0);
+    const uint32_t tok = orc_argmax_top1(lg, vocab);
+    if (lg != logits) free(lg);
+    free(xn);
+    return tok;
 }

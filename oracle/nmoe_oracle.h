@@ -112,6 +112,26 @@ int orc_moe_block_forward(const orc_layer *L, int k, const float *x, const float
 int orc_moe_block_forward_batched(const orc_layer *L, int T, int k, const float *x,
                                   const float *h_mid, float *out, uint32_t *idx, float *w);
 
+
+/* RMSNorm as the reference's nmoe_rms_norm kernel computes it (metal/kernels.metal:862-900):
+ * out = x * rsqrt(mean(x^2) + eps) * (w (+1 if add_one)); w NULL = unit weight. The sum of
+ * squares is taken in double here. Cross-checked against the CPU form nmoe_cpu_rms_norm
+ * (src/math.m:34-64, x / sqrt(mean + eps) * w). */
+void orc_rms_norm(const float *x, const uint16_t *w_bf16, float *out, size_t n, float eps, int add_one);
+
+/* Top-1 rule of nmoe_argmax_top1 / nmoe_lm_head_argmax_reduce (metal/kernels.metal:1562-1597,
+ * 1668-1713): lowest index of the maximum among values > -FLT_MAX (NaN never wins); 0 if none. */
+uint32_t orc_argmax_top1(const float *v, size_t n);
+
+/* LM head of NMOERunLmHeadArgmaxQ4Metal (src/runtime.m:1882-1948; kernels.metal:1599-1713):
+ * optional RMSNorm of x (norm_w non-NULL), logits[r] = kernel-form dequant matvec (form 0,
+ * lane-strided, as nmoe_lm_head_argmax_q4 accumulates), token = orc_argmax_top1(logits).
+ * dtype ORC_DTYPE_Q4 (w u32 [vocab][in/8], s/b bf16 [vocab][in/64]) or ORC_DTYPE_BF16
+ * (w bf16 [vocab][in]). logits may be NULL only if the caller does not need them. */
+uint32_t orc_lm_head_argmax(int dtype, const void *w, const uint16_t *s, const uint16_t *b, size_t vocab,
+                            size_t in_dim, const float *x, const uint16_t *norm_w, float eps, int add_one,
+                            float *logits);
+
 /* Set the OpenMP thread count used by the matvecs (0 = library default). */
 void orc_set_threads(int n);
 int orc_get_threads(void);

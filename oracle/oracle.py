@@ -82,6 +82,12 @@ def lib() -> C.CDLL:
         L.orc_moe_block_forward_batched.restype = C.c_int
         L.orc_moe_block_forward_batched.argtypes = [C.POINTER(OrcLayer), C.c_int, C.c_int, _f32p, C.c_void_p,
                                                     _f32p, C.c_void_p, C.c_void_p]
+        L.orc_rms_norm.argtypes = [_f32p, C.c_void_p, _f32p, C.c_size_t, C.c_float, C.c_int]
+        L.orc_argmax_top1.restype = C.c_uint32
+        L.orc_argmax_top1.argtypes = [_f32p, C.c_size_t]
+        L.orc_lm_head_argmax.restype = C.c_uint32
+        L.orc_lm_head_argmax.argtypes = [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t,
+                                         _f32p, C.c_void_p, C.c_float, C.c_int, C.c_void_p]
         L.orc_set_threads.argtypes = [C.c_int]
         L.orc_get_threads.restype = C.c_int
         _lib = L
@@ -101,6 +107,7 @@ def ref_lib():
     L.nmoe_cpu_sigmoid.restype = C.c_float
     L.nmoe_cpu_sigmoid.argtypes = [C.c_float]
     L.nmoe_cpu_dequant_matvec.argtypes = [_u32p, _u16p, _u16p, _f32p, _f32p, C.c_size_t, C.c_size_t, C.c_int]
+    L.nmoe_cpu_rms_norm.argtypes = [_f32p, C.c_void_p, _f32p, C.c_size_t, C.c_float, C.c_int]
     L.nmoe_f32_to_bf16.restype = C.c_uint16
     L.nmoe_f32_to_bf16.argtypes = [C.c_float]
     return L
@@ -276,3 +283,50 @@ def route_reference(logits: np.ndarray, k: int):
     n = L.orc_topk(p, p.size, k, idx, vals)
     L.orc_renormalize(vals, n)
     return idx[:n], vals[:n]
+
+
+# ------------------------------------------------------------------ LM head ----
+
+def rms_norm(x: np.ndarray, w_bf16: np.ndarray | None, eps: float = 1e-6, add_one: bool = True) -> np.ndarray:
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty_like(x)
+    w = None if w_bf16 is None else np.ascontiguousarray(w_bf16, np.uint16)
+    lib().orc_rms_norm(x, None if w is None else w.ctypes.data, out, x.size, eps, int(add_one))
+    return out
+
+
+def argmax_top1(v: np.ndarray) -> int:
+    return int(lib().orc_argmax_top1(np.ascontiguousarray(v, np.float32), v.size))
+
+
+@dataclass
+class LmHead:
+    """Synthetic LM head (lm_head.weight [vocab][2048]) in the converter's q4 form or bf16."""
+    dtype: int
+    vocab: int
+    weight: np.ndarray                 # q4: u32 [vocab][256]; bf16: u16 [vocab][2048]
+    scales: np.ndarray | None = None   # q4: u16 [vocab][32]
+    biases: np.ndarray | None = None
+
+
+def make_lm_head(seed: int, vocab: int, dtype: int = DTYPE_Q4, std: float = 0.02) -> LmHead:
+    rng = np.random.default_rng(seed)
+    w = randn_bf16(rng, (vocab, HIDDEN), std)
+    if dtype == DTYPE_BF16:
+        return LmHead(dtype, vocab, w)
+    p, sc, b = quantize_rows(w, 4)
+    return LmHead(dtype, vocab, p, sc, b)
+
+
+def lm_head_argmax(head: LmHead, x: np.ndarray, norm_w: np.ndarray | None = None, eps: float = 1e-6,
+                   add_one: bool = True):
+    """(token, logits fp32[vocab]) by the reference's head and top-1 rule."""
+    x = np.ascontiguousarray(x, np.float32)
+    logits = np.empty(head.vocab, np.float32)
+    nw = None if norm_w is None else np.ascontiguousarray(norm_w, np.uint16)
+    tok = lib().orc_lm_head_argmax(head.dtype, head.weight.ctypes.data,
+                                   None if head.scales is None else head.scales.ctypes.data,
+                                   None if head.biases is None else head.biases.ctypes.data,
+                                   head.vocab, HIDDEN, x, None if nw is None else nw.ctypes.data, eps,
+                                   int(add_one), logits.ctypes.data)
+    return int(tok), logits
