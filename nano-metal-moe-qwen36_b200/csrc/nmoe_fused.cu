@@ -60,6 +60,7 @@ constexpr int kXP = 36;   // padded floats per 32 columns (conflict-free 16-byte
 constexpr int kMaxUnits = 4;
 constexpr uint32_t kUnset = 0xFFFFFFFFu;   // top-k slot not decided yet
 constexpr int kTlSlots = 32;
+constexpr int kLogitCopies = 8;
 // mbarriers: router rows, shared expert, then per routed unit its gate/up part (band pair
 // + scales) and its down part (word columns + group scales/biases)
 constexpr int kBarRouter = 0, kBarShared = 1, kBarGu0 = 2, kBarD0 = kBarGu0 + kMaxUnits, kNumBars = kBarD0 + kMaxUnits;
@@ -71,7 +72,9 @@ struct FusedSync {
     uint32_t pad1[31];
     uint32_t inited;                 // output-row initialisations of all launches (+G per launch)
     uint32_t pad3[31];
-    uint64_t logits[kExperts];       // tagged {tag, value}
+    // tagged {tag, value} logits in kLogitCopies copies: CTA c reads copy c % kLogitCopies,
+    // so that the 148 reads that follow the last publication spread over 8x the L2 lines
+    uint64_t logits[kLogitCopies][kExperts];
     uint32_t diag[1024];             // per CTA: highest phase reached; 100+phase where a wait gave up
     uint32_t tl[1024][kTlSlots];     // per CTA phase timestamps (globaltimer low 32 bits)
 };
@@ -141,7 +144,11 @@ __device__ __forceinline__ bool poll_tagged8(const uint64_t *p, uint32_t tag, fl
     }
 }
 
-__device__ __forceinline__ int split_lo(int total, int parts, int i) { return (int)((long long)total * i / parts); }
+// total * i < 2^32 for every split here (total <= 2048, i <= grid <= 1024): 32-bit unsigned
+// division, inline (a 64-bit division is a called routine, slow on a cold instruction cache)
+__device__ __forceinline__ int split_lo(int total, int parts, int i) {
+    return (int)(((uint32_t)total * (uint32_t)i) / (uint32_t)parts);
+}
 __device__ __forceinline__ void set_err(int *err, int code) { atomicCAS(err, 0, code); }
 
 __device__ __forceinline__ void red_add_v4(float *p, float a, float b, float c, float d) {
@@ -525,9 +532,10 @@ __device__ __forceinline__ void down_units(const uint8_t *const *wc, const uint1
 // The routing selection (one copy: run dry by warp 4, then for real by warp 0; warps 0
 // and 4 share an SM sub-partition and its instruction cache).
 __device__ __noinline__ float route_topk(float v0, float v1, float v2, float v3, float v4, float v5, float v6,
-                                         float v7, int k, int lane, uint32_t *sidx, float *sval) {
+                                         float v7, int k, int lane, uint32_t *sidx, float *sval,
+                                         uint32_t *tl) {
     const float v[8] = {v0, v1, v2, v3, v4, v5, v6, v7};
-    return warp_topk_smem(v, k, lane, sidx, sval);
+    return warp_topk_smem(v, k, lane, sidx, sval, tl);
 }
 
 #define NMOE_STAMP(slot)                                                    \
@@ -578,6 +586,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
     const bool do_shared = !P.route_only && nS > 0;
     // q4 shared down: the groups of 64 columns that rows [s0, s0+nS) fall in
     const int sg0 = s0 >> 6, nsg = nS > 0 ? ((s0 + nS - 1) >> 6) - sg0 + 1 : 0;
+    uint32_t tl_a = 0, tl_b = 0, tl_c = 0;
+    if (kTL) tl_a = (uint32_t)globaltimer_ns();
     // Programmatic dependent launch: the next call on this stream may start launching now;
     // its CTAs become resident as this call's CTAs exit.
     if (tid == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -594,11 +604,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
     }
     if (kTL && tid < kTlSlots) sy->tl[c & 1023][tid] = 0;   // this launch's stamps only
     __syncthreads();
+    if (kTL) tl_b = (uint32_t)globaltimer_ns();
 
     // ---- 0. routing-independent copies ------------------------------------------------
     // Weights depend on nothing the previous call on this stream produces: the router rows
-    // and the shared-expert rows and columns go out before the dependency wait (router
-    // first). x, h_mid, out and the sync state are touched only after the wait.
+    // go out before the dependency wait, the shared-expert rows and columns right after
+    // the x request. x, h_mid, out and the sync state are touched only after the wait.
     const uint64_t pol0 = policy_evict_first();
     auto issue_shared = [&]() {
         if (do_shared) {
@@ -618,10 +629,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
         mbar_arrive_expect_tx(&bars[kBarRouter], nR * RW);
         if (nR) bulk_g2s(sm + Y.rw, P.router + (size_t)r0 * RW, nR * RW, &bars[kBarRouter], pol0);
         S->armed = (1u << kBarRouter) | (do_shared ? 1u << kBarShared : 0u);
-        issue_shared();
     }
+    if (kTL) tl_c = (uint32_t)globaltimer_ns();
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    if (kTL && tid == 0) NMOE_STAMP(16);
+    if (kTL && tid == 0) {
+        NMOE_STAMP(16);
+        sy->tl[c & 1023][29] = tl_a;
+        sy->tl[c & 1023][30] = tl_b;
+        sy->tl[c & 1023][31] = tl_c;
+    }
     uint32_t tag;
     asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(tag) : "l"(&sy->epoch) : "memory");
     tag += 1u;
@@ -634,6 +650,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
         xr4.x = u.x;
         xr4.y = u.y;
     }
+    // the shared expert's 6 MB go out behind the x request, not ahead of it (x gates the
+    // router dots; the shared rows are needed only after them)
+    if (tid == 0) issue_shared();
     // this CTA's output rows start at h_mid (or 0); every CTA adds its partials once all
     // logits are published, i.e. after every CTA has written its rows
     if (kTL && tid == 0) sy->tl[c & 1023][0] = (uint32_t)t_start;
@@ -661,6 +680,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
             for (int o2 = 16; o2 > 0; o2 >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o2));
             if (lane == 0) atomicMax(&S->xmax_bits, __float_as_uint(m));
         }
+        if (kTL && tid == 0) NMOE_STAMP(21);
         if ((tid & 7) == 0) {
             const int cc = col0 >> 5;
             xsum[3 * cc] = e;
@@ -709,7 +729,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
                     for (int r = 0; r < nR; ++r) {
                         float t = 0.f;
                         for (int q = 0; q < kRSeg; ++q) t += rpart[r * kRSeg + q];
-                        st_tagged(&sy->logits[r0 + r], t, tag);
+#pragma unroll
+                        for (int cp = 0; cp < kLogitCopies; ++cp) st_tagged(&sy->logits[cp][r0 + r], t, tag);
                     }
                     // a count of the publications, for the pollers (the tags above stay the
                     // authority: a poller that reads the count early re-reads the words)
@@ -770,7 +791,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
                         // sub-partition, so warp 0's real pass finds the code cached.
                         const float *d = xs + 8 * lane;
                         const float l0 = route_topk(d[0], d[1], d[2], d[3], d[4], d[5], d[6], d[7], k, lane,
-                                                    S->dsidx, S->dsval);
+                                                    S->dsidx, S->dsval, nullptr);
                         if (lane == 0) S->sink[warp] = l0;
                     }
                 }
@@ -811,9 +832,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
             for (uint32_t it = 0; (int)(ld_relaxed_u32(&sy->arrive) - target) < 0; ++it)
                 if (it >= kMaxSpins || globaltimer_ns() > deadline) break;
         }
+        if (kTL && lane == 0) NMOE_STAMP(22);
         __syncwarp();
         // normally one read: every tag is already this launch's
-        if (ok) ok = poll_tagged8(&sy->logits[8 * lane], want, v, deadline);
+        if (ok) ok = poll_tagged8(&sy->logits[c % kLogitCopies][8 * lane], want, v, deadline);
         ok = __all_sync(0xffffffffu, ok);
         if (kTL && lane == 0) NMOE_STAMP(15);
         if (!ok) {
@@ -825,7 +847,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
             }
             // each round's winner writes S->sidx[r]; warp 1 issues a unit's copies as soon
             // as its slot is decided
-            const float l0 = route_topk(v[0], v[1], v[2], v[3], v[4], v[5], v[6], v[7], k, lane, S->sidx, S->sval);
+            if (kTL && lane == 0) NMOE_STAMP(23);
+            const float l0 = route_topk(v[0], v[1], v[2], v[3], v[4], v[5], v[6], v[7], k, lane, S->sidx, S->sval,
+                                        kTL ? &sy->tl[c & 1023][24] : nullptr);
             if (kTL && lane == 0) NMOE_STAMP(6);
             const uint32_t e = lane < k ? S->sidx[lane & 7] : 0u;
             const int valid = lane < k && e < (uint32_t)P.num_experts;
@@ -964,7 +988,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
                 }
                 if (lane == 0)
                     for (int n = 0; n < nb; ++n) uact[(i + n) * 16 + warp] = live[n] ? act[n] : 0.f;
+                if (i == 0 && tid == 0) NMOE_STAMP(27);
                 __syncthreads();
+                if (i == 0 && tid == 0) NMOE_STAMP(28);
                 if (warp == 0) {
                     if (nb == 2) units_tables<kBits, 2>(uact + i * 16, uas + i, lane);
                     else units_tables<kBits, 1>(uact + i * 16, uas + i, lane);
@@ -972,6 +998,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_moe_decode_fused(const FusedPar
                 bool okd = true;
                 for (int n = 0; n < nb; ++n) okd &= mbar_wait_warp(&bars[kBarD0 + i + n], 0, deadline);
                 if (!okd && lane == 0) NMOE_GIVEUP(4);
+                if (i == 0 && tid == 0) NMOE_STAMP(26);
                 __syncthreads();
                 if (i == 0 && tid == 0) NMOE_STAMP(14);
                 const uint8_t *wc[2] = {up[0] + pg.bp, up[1] + pg.bp};

@@ -83,7 +83,10 @@ __device__ __forceinline__ TopkLane warp_topk_lane(const float *v, int k, int la
 // a __syncwarp), so a round is one warp max, one ballot and the pop; the winner is the
 // lowest lane holding the maximum (no lane index is moved between lanes). Returns the
 // largest logit (l0) on every lane.
-__device__ __forceinline__ float warp_topk_smem(const float *v, int k, int lane, uint32_t *sidx, float *sval) {
+// tl (diagnostic timeline, may be null): lane 0 stamps %globaltimer after the per-lane
+// sort (tl[0]) and after the first round (tl[1]).
+__device__ __forceinline__ float warp_topk_smem(const float *v, int k, int lane, uint32_t *sidx, float *sval,
+                                               uint32_t *tl = nullptr) {
     uint32_t key[8], id[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
@@ -103,6 +106,11 @@ __device__ __forceinline__ float warp_topk_smem(const float *v, int k, int lane,
         }
     uint32_t lt;
     asm("mov.u32 %0, %%lanemask_lt;" : "=r"(lt));
+    if (tl != nullptr && lane == 0) {
+        uint64_t t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t) : "r"(key[7]), "r"(key[0]));
+        tl[0] = (uint32_t)t;
+    }
     float l0 = 0.f;
 #pragma unroll 1
     for (int r = 0; r < k; ++r) {
@@ -120,6 +128,11 @@ __device__ __forceinline__ float warp_topk_smem(const float *v, int k, int lane,
             id[j] = me ? id[j + 1] : id[j];
         }
         key[7] = me ? 0u : key[7];
+        if (r == 0 && tl != nullptr && lane == 0) {
+            uint64_t t;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t) : "r"(key[0]));
+            tl[1] = (uint32_t)t;
+        }
     }
     __syncwarp();
     return l0;

@@ -16,7 +16,7 @@ import subprocess
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libnmoe_cuda.so")
+LIB_PATH = os.environ.get("NMOE_LIB") or os.path.join(HERE, "libnmoe_cuda.so")   # NMOE_LIB: another build
 
 OK, EINVAL, ESIZE, ECUDA, ENCCL, ETIMEOUT, EDEVICE, EIO, ENOMEM = range(9)
 DTYPE_F32, DTYPE_BF16, DTYPE_Q2, DTYPE_Q4 = 0, 1, 2, 4
@@ -176,7 +176,9 @@ def _np_ptr(a) -> int | None:
 # Stamp slots of the batch-1 kernel's timeline (k_moe_decode_fused, NMOE_TIMELINE=1).
 TIMELINE_WIDTH = 32
 TIMELINE_SLOTS = {
+    29: "prologue: indices computed", 30: "prologue: barriers initialised", 31: "prologue: copies issued",
     16: "dependency wait done",
+    21: "x loaded (tid 0)",
     1: "x staged",
     18: "router rows ready (warp 0)",
     19: "router dot done (warp 0)",
@@ -184,7 +186,11 @@ TIMELINE_SLOTS = {
     8: "logits published",
     2: "router and shared rows done",
     13: "logits poll starts",
+    22: "publication count complete",
     15: "logits seen",
+    23: "top-k starts",
+    24: "top-k lane sort done",
+    25: "top-k round 0 done",
     6: "top-k ids done",
     17: "unit 0 copies issued",
     10: "routed copies issued",
@@ -192,6 +198,9 @@ TIMELINE_SLOTS = {
     3: "routing barrier",
     12: "shared down done",
     11: "first unit landed",
+    27: "warp 0 gate/up dots done (units 0-1)",
+    28: "all warps' gate/up dots done (units 0-1)",
+    26: "down columns landed (units 0-1)",
     14: "unit 0 gate/up done",
     5: "routed units done",
     7: "end",
