@@ -672,6 +672,7 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.empty_cache()
     if args.lm_head and rank == 0:
         result["lm_head"] = run_lm_head(args, dev)
+        result["layer_crc32c"] = run_crc(args, dev)
     if args.ep_tokens > 0:
         ep = run_ep_batched(args, rank, world, dev)
         if result is not None:
@@ -761,6 +762,43 @@ def run_lm_head(args, dev):
     return out
 
 
+def run_crc(args, dev):
+    """Device CRC-32C of one q4 layer image (256 expert blobs, 453 MB, in HBM) against the
+    host CRC-32C (SSE4.2, one core) of the same bytes; both checked against each other."""
+    import torch
+    import nmoe_b200 as N
+    from oracle import oracle as O
+    lw = O.make_layer(args.seed + 9, bits=4, distinct_experts=8)
+    img = lw.experts.view(np.uint8)
+    esz = N.expert_size(4)
+    d = torch.from_numpy(img.view(np.int32)).to(f"cuda:{dev}")
+    out = torch.zeros(256, dtype=torch.int32, device=f"cuda:{dev}")
+    st = torch.cuda.Stream(device=dev)
+    for _ in range(3):
+        N.crc32c_device(d, esz, 256, out, stream=st.cuda_stream)
+    torch.cuda.synchronize()
+    reps = 10
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        N.crc32c_device(d, esz, 256, out, stream=st.cuda_stream)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    t0 = time.perf_counter()
+    host = N.expert_crcs(img, 4)
+    host_s = time.perf_counter() - t0
+    dev_crc = out.cpu().numpy().view(np.uint32)
+    if not np.array_equal(dev_crc, host):
+        raise RuntimeError("device CRC-32C disagrees with the host")
+    pk, pk_kind = peaks()
+    gbs = img.nbytes / (ms * 1e-3) / 1e9
+    return {"bytes": int(img.nbytes), "device_ms": ms, "device_gbs": gbs, "frac_of_hbm": gbs / pk,
+            "peak_kind": pk_kind, "host_sse42_one_core_ms": host_s * 1e3,
+            "host_gbs": img.nbytes / host_s / 1e9,
+            "note": "load-time integrity check (nmoe_moe_load_layer_checked), not on the decode path"}
+
+
 def run_ep_batched(args, rank, world, dev):
     """Config 2 beside the decode line, at every N: T tokens per rank (--ep-tokens) through
     --ep-layers resident layers per step, experts sharded 256/N per GPU with token rows
@@ -838,7 +876,7 @@ def main():
     ap.add_argument("--pool", type=int, default=32, help="distinct expert packs generated on the host")
     ap.add_argument("--seed", type=int, default=2026)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--workload", choices=["decode", "batched", "lm_head"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "batched", "lm_head", "crc"], default="decode")
     ap.add_argument("--lm-dtypes", default="q4,bf16", help="LM head weight types timed (q4, bf16)")
     ap.add_argument("--bits", type=int, choices=[2, 4], default=4, help="decode: expert packs (4: config 0, 2: config 1)")
     ap.add_argument("--k", type=int, default=8, help="decode: routed experts per token (config 1 sweeps 1..8)")
@@ -871,7 +909,11 @@ def main():
         import torch.distributed as dist
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local_rank}"))
-    if args.workload == "lm_head":
+    if args.workload == "crc":
+        import torch
+        torch.cuda.set_device(local_rank)
+        res = {"workload": "crc", **run_crc(args, local_rank)} if rank == 0 else None
+    elif args.workload == "lm_head":
         import torch
         torch.cuda.set_device(local_rank)
         res = {"workload": "lm_head", **run_lm_head(args, local_rank)} if rank == 0 else None

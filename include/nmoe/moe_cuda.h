@@ -43,6 +43,7 @@ extern "C" {
 #define NMOE_EDEVICE 6  /* the device error word was set (e.g. routed expert id >= experts)   */
 #define NMOE_EIO 7      /* file open/read error                                               */
 #define NMOE_ENOMEM 8   /* allocation failure                                                 */
+#define NMOE_ECHECKSUM 9 /* an expert pack's CRC-32C differs from the expected one          */
 
 /* ---- dtypes ------------------------------------------------------------------- */
 #define NMOE_DTYPE_F32 0
@@ -139,6 +140,28 @@ const char *nmoe_moe_last_error(const nmoe_moe_ctx *ctx);
 int nmoe_moe_load_layer(nmoe_moe_ctx *ctx, int layer, const void *layer_bin, size_t bytes);
 /* Same, reading the file at `path` (e.g. packed_experts/layer_07.bin). */
 int nmoe_moe_load_layer_file(nmoe_moe_ctx *ctx, int layer, const char *path);
+/* No counterpart in the reference (its loader checks sizes only, src/expert_io.m:52-65).
+ * The loads above with an integrity check: the CRC-32C (Castagnoli, reflected 0x82F63B78,
+ * init and final xor 0xFFFFFFFF) of every expert blob this context holds is computed on
+ * the device while the image is staged, before it is repacked. expected_crc[num_experts]
+ * (global expert ids, may be NULL): on the first mismatch nothing is loaded and the call
+ * returns NMOE_ECHECKSUM, naming the expert in nmoe_moe_last_error(). crc_out[num_experts]
+ * (may be NULL) receives the CRCs (entries of experts an expert-parallel rank does not
+ * hold are left untouched). nmoe_crc32c() gives the same values on the host. */
+int nmoe_moe_load_layer_checked(nmoe_moe_ctx *ctx, int layer, const void *layer_bin, size_t bytes,
+                                const uint32_t *expected_crc, uint32_t *crc_out);
+int nmoe_moe_load_layer_file_checked(nmoe_moe_ctx *ctx, int layer, const char *path,
+                                     const uint32_t *expected_crc, uint32_t *crc_out);
+/* Host CRC-32C, continuing from `crc` (0 to start): nmoe_crc32c(0, blob, n) is the value
+ * the checked loads compute for a blob. SSE4.2 instruction where the CPU has it. */
+uint32_t nmoe_crc32c(uint32_t crc, const void *data, size_t n);
+/* Device CRC-32C of nblobs consecutive blobs of blob_bytes each (a multiple of 8192;
+ * expert blobs are) in caller-owned DEVICE memory (8-byte aligned) into d_crc_out[nblobs]
+ * (device). Asynchronous on `stream`, allocates nothing: e.g. to verify the device copy of
+ * a layer image that nmoe_moe_forward_static reads. One CTA per blob. */
+int nmoe_crc32c_device(const void *d_data, size_t blob_bytes, int nblobs, uint32_t *d_crc_out, void *stream);
+/* CRC-32C of A followed by B from crc(A), crc(B) and the length of B in bytes. */
+uint32_t nmoe_crc32c_combine(uint32_t crc_a, uint32_t crc_b, size_t len_b);
 /* Upload one layer's router + shared-expert weights (dtypes from the config). */
 int nmoe_moe_set_dense(nmoe_moe_ctx *ctx, int layer, const nmoe_moe_dense_weights *w);
 

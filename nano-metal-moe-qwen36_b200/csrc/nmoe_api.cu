@@ -18,6 +18,10 @@
 
 using namespace nmoe;
 
+namespace nmoe {
+cudaError_t crc32c_blobs(const uint8_t *d_base, size_t blob, int n, uint32_t *d_out, cudaStream_t st);
+}
+
 // ------------------------------------------------------------------ helpers ----
 
 void nmoe_ctx_set_error(nmoe_moe_ctx *ctx, const char *fmt, ...) {
@@ -78,6 +82,7 @@ extern "C" const char *nmoe_moe_strerror(int status) {
         case NMOE_EDEVICE: return "device error word set";
         case NMOE_EIO: return "I/O error";
         case NMOE_ENOMEM: return "out of memory";
+        case NMOE_ECHECKSUM: return "checksum mismatch";
         default: return "unknown status";
     }
 }
@@ -204,7 +209,37 @@ static cudaError_t repack_layer(nmoe_moe_ctx *ctx, int layer, const uint8_t *sta
     return e;
 }
 
-extern "C" int nmoe_moe_load_layer(nmoe_moe_ctx *ctx, int layer, const void *layer_bin, size_t bytes) {
+// CRC-32C of this rank's staged experts, checked against expected[] (global expert ids)
+// and written to crc_out[] (global ids; entries of experts this rank does not hold are
+// left as they are). NMOE_ECHECKSUM names the first mismatching expert.
+static int check_staged(nmoe_moe_ctx *ctx, int layer, const uint8_t *d_stage, const uint32_t *expected,
+                        uint32_t *crc_out) {
+    if (expected == nullptr && crc_out == nullptr) return NMOE_OK;
+    uint32_t *d_crc = nullptr;
+    NMOE_CUDA_TRY(ctx, cudaMalloc(&d_crc, (size_t)ctx->n_local * sizeof(uint32_t)));
+    std::vector<uint32_t> h(ctx->n_local);
+    cudaError_t e = crc32c_blobs(d_stage, ctx->esz, ctx->n_local, d_crc, 0);
+    if (e == cudaSuccess) e = cudaMemcpy(h.data(), d_crc, h.size() * sizeof(uint32_t), cudaMemcpyDeviceToHost);
+    cudaFree(d_crc);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "crc32c");
+    for (int i = 0; i < ctx->n_local; ++i) {
+        const int ge = ctx->expert_lo + i;
+        if (crc_out) crc_out[ge] = h[i];
+    }
+    if (expected)
+        for (int i = 0; i < ctx->n_local; ++i) {
+            const int ge = ctx->expert_lo + i;
+            if (h[i] != expected[ge]) {
+                nmoe_ctx_set_error(ctx, "layer %d expert %d: CRC-32C 0x%08x, expected 0x%08x", layer, ge, h[i],
+                                   expected[ge]);
+                return NMOE_ECHECKSUM;
+            }
+        }
+    return NMOE_OK;
+}
+
+extern "C" int nmoe_moe_load_layer_checked(nmoe_moe_ctx *ctx, int layer, const void *layer_bin, size_t bytes,
+                                           const uint32_t *expected_crc, uint32_t *crc_out) {
     if (ctx == nullptr) return NMOE_EINVAL;
     if (layer < 0 || layer >= ctx->cfg.num_layers) {
         nmoe_ctx_set_error(ctx, "layer %d out of range [0, %d)", layer, ctx->cfg.num_layers);
@@ -221,14 +256,26 @@ extern "C" int nmoe_moe_load_layer(nmoe_moe_ctx *ctx, int layer, const void *lay
     uint8_t *stage = nullptr;
     NMOE_CUDA_TRY(ctx, cudaMalloc(&stage, ctx->expert_layer_bytes));
     cudaError_t e = cudaMemcpy(stage, src, ctx->expert_layer_bytes, cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = repack_layer(ctx, layer, stage);
+    if (e != cudaSuccess) {
+        cudaFree(stage);
+        return cuda_fail(ctx, e, "load_layer");
+    }
+    int rc = check_staged(ctx, layer, stage, expected_crc, crc_out);
+    if (rc == NMOE_OK) {
+        e = repack_layer(ctx, layer, stage);
+        if (e != cudaSuccess) rc = cuda_fail(ctx, e, "load_layer");
+    }
     cudaFree(stage);
-    if (e != cudaSuccess) return cuda_fail(ctx, e, "load_layer");
-    ctx->loaded[layer] = 1;
-    return NMOE_OK;
+    if (rc == NMOE_OK) ctx->loaded[layer] = 1;
+    return rc;
 }
 
-extern "C" int nmoe_moe_load_layer_file(nmoe_moe_ctx *ctx, int layer, const char *path) {
+extern "C" int nmoe_moe_load_layer(nmoe_moe_ctx *ctx, int layer, const void *layer_bin, size_t bytes) {
+    return nmoe_moe_load_layer_checked(ctx, layer, layer_bin, bytes, nullptr, nullptr);
+}
+
+extern "C" int nmoe_moe_load_layer_file_checked(nmoe_moe_ctx *ctx, int layer, const char *path,
+                                                const uint32_t *expected_crc, uint32_t *crc_out) {
     if (ctx == nullptr || path == nullptr) return NMOE_EINVAL;
     if (layer < 0 || layer >= ctx->cfg.num_layers) {
         nmoe_ctx_set_error(ctx, "layer %d out of range [0, %d)", layer, ctx->cfg.num_layers);
@@ -268,6 +315,7 @@ extern "C" int nmoe_moe_load_layer_file(nmoe_moe_ctx *ctx, int layer, const char
     }
     cudaFreeHost(stage);
     fclose(f);
+    if (rc == NMOE_OK) rc = check_staged(ctx, layer, dst, expected_crc, crc_out);
     if (rc == NMOE_OK) {
         cudaError_t e = repack_layer(ctx, layer, dst);
         if (e != cudaSuccess) rc = cuda_fail(ctx, e, "repack");
@@ -275,6 +323,10 @@ extern "C" int nmoe_moe_load_layer_file(nmoe_moe_ctx *ctx, int layer, const char
     cudaFree(dst);
     if (rc == NMOE_OK) ctx->loaded[layer] = 1;
     return rc;
+}
+
+extern "C" int nmoe_moe_load_layer_file(nmoe_moe_ctx *ctx, int layer, const char *path) {
+    return nmoe_moe_load_layer_file_checked(ctx, layer, path, nullptr, nullptr);
 }
 
 extern "C" int nmoe_moe_set_dense(nmoe_moe_ctx *ctx, int layer, const nmoe_moe_dense_weights *w) {

@@ -18,7 +18,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("NMOE_LIB") or os.path.join(HERE, "libnmoe_cuda.so")   # NMOE_LIB: another build
 
-OK, EINVAL, ESIZE, ECUDA, ENCCL, ETIMEOUT, EDEVICE, EIO, ENOMEM = range(9)
+OK, EINVAL, ESIZE, ECUDA, ENCCL, ETIMEOUT, EDEVICE, EIO, ENOMEM, ECHECKSUM = range(10)
 DTYPE_F32, DTYPE_BF16, DTYPE_Q2, DTYPE_Q4 = 0, 1, 2, 4
 HIDDEN, INTER, NUM_EXPERTS, GROUP, MAX_K = 2048, 512, 256, 64, 8
 
@@ -32,6 +32,8 @@ ABI_SYMBOLS = (
     "nmoe_moe_debug_logits", "nmoe_moe_debug_gemm_trace", "nmoe_moe_nccl_unique_id", "nmoe_moe_decode_grid",
     "nmoe_moe_static_scratch_bytes", "nmoe_moe_static_status", "nmoe_moe_debug_ep_times",
     "nmoe_lm_head_argmax", "nmoe_lm_head_workspace_bytes", "nmoe_lm_head_error",
+    "nmoe_moe_load_layer_checked", "nmoe_moe_load_layer_file_checked", "nmoe_crc32c", "nmoe_crc32c_combine",
+    "nmoe_crc32c_device",
 )
 
 
@@ -125,6 +127,16 @@ def lib() -> C.CDLL:
     L.nmoe_moe_nccl_unique_id.argtypes = [vp, sz]
     L.nmoe_moe_debug_gemm_trace.restype = i
     L.nmoe_moe_debug_gemm_trace.argtypes = [vp, vp, i]
+    L.nmoe_moe_load_layer_checked.restype = i
+    L.nmoe_moe_load_layer_checked.argtypes = [vp, i, vp, sz, vp, vp]
+    L.nmoe_moe_load_layer_file_checked.restype = i
+    L.nmoe_moe_load_layer_file_checked.argtypes = [vp, i, C.c_char_p, vp, vp]
+    L.nmoe_crc32c.restype = C.c_uint32
+    L.nmoe_crc32c.argtypes = [C.c_uint32, vp, sz]
+    L.nmoe_crc32c_device.restype = i
+    L.nmoe_crc32c_device.argtypes = [vp, sz, i, vp, vp]
+    L.nmoe_crc32c_combine.restype = C.c_uint32
+    L.nmoe_crc32c_combine.argtypes = [C.c_uint32, C.c_uint32, sz]
     L.nmoe_lm_head_argmax.restype = i
     L.nmoe_lm_head_argmax.argtypes = [C.POINTER(Tensor), i, i, i, vp, i, vp, C.c_float, i, vp, vp, vp, vp]
     L.nmoe_lm_head_workspace_bytes.restype = sz
@@ -270,6 +282,22 @@ class Context:
     def load_layer_file(self, layer: int, path: str):
         self._check(self._L.nmoe_moe_load_layer_file(self.h, layer, path.encode()))
 
+    def load_layer_checked(self, layer: int, layer_bin: np.ndarray, expected=None):
+        """Load with the device CRC-32C check; returns the per-expert CRCs (uint32[num_experts])."""
+        a = np.ascontiguousarray(layer_bin).view(np.uint8)
+        out = np.zeros(self.cfg.num_experts, np.uint32)
+        exp = None if expected is None else np.ascontiguousarray(expected, np.uint32)
+        self._check(self._L.nmoe_moe_load_layer_checked(self.h, layer, a.ctypes.data, a.nbytes,
+                                                        _np_ptr(exp), out.ctypes.data))
+        return out
+
+    def load_layer_file_checked(self, layer: int, path: str, expected=None):
+        out = np.zeros(self.cfg.num_experts, np.uint32)
+        exp = None if expected is None else np.ascontiguousarray(expected, np.uint32)
+        self._check(self._L.nmoe_moe_load_layer_file_checked(self.h, layer, path.encode(), _np_ptr(exp),
+                                                             out.ctypes.data))
+        return out
+
     def set_dense(self, layer: int, router: dict, shared_gate: dict, shared_up: dict, shared_down: dict,
                   shared_gate_vec: dict):
         """Each dict: {"weight": ndarray, ["scales": ndarray, "biases": ndarray]}."""
@@ -384,3 +412,26 @@ def lm_head_argmax(head: dict, head_dtype: int, vocab: int, x, token_out, worksp
                                _ptr(workspace), stream)
     if rc != OK:
         raise NmoeError(rc, L.nmoe_lm_head_error().decode())
+
+
+def crc32c(data, crc: int = 0) -> int:
+    """nmoe_crc32c: host CRC-32C of a bytes-like / numpy buffer."""
+    a = np.ascontiguousarray(np.frombuffer(data, np.uint8) if isinstance(data, (bytes, bytearray)) else data)
+    return int(lib().nmoe_crc32c(crc, a.ctypes.data, a.nbytes))
+
+
+def expert_crcs(layer_bin: np.ndarray, bits: int):
+    """Per-expert CRC-32C of a layer_XX.bin image (host): the values the checked loads
+    compute on the device, e.g. to write a manifest next to the file."""
+    a = np.ascontiguousarray(layer_bin).view(np.uint8)
+    esz = expert_size(bits)
+    if esz == 0 or a.nbytes % esz:
+        raise ValueError("image size is not a whole number of expert blobs")
+    return np.array([crc32c(a[i * esz:(i + 1) * esz]) for i in range(a.nbytes // esz)], np.uint32)
+
+
+def crc32c_device(data, blob_bytes: int, nblobs: int, out, stream=0):
+    """nmoe_crc32c_device: CRC-32C of nblobs device blobs into the device uint32 tensor `out`."""
+    rc = lib().nmoe_crc32c_device(_ptr(data), blob_bytes, nblobs, _ptr(out), stream)
+    if rc != OK:
+        raise NmoeError(rc, "nmoe_crc32c_device")

@@ -498,3 +498,14 @@ uint32_t orc_lm_head_argmax(int dtype, const void *w, const uint16_t *s, const u
     free(xn);
     return tok;
 }
+
+/* ------------------------------------------------------------- CRC-32C ---- */
+
+uint32_t orc_crc32c(uint32_t crc, const uint8_t *data, size_t n) {
+    crc = ~crc;
+    for (size_t i = 0; i < n; i++) {
+        crc ^= data[i];
+        for (int b = 0; b < 8; b++) crc = (crc & 1u) ? (crc >> 1) ^ 0x82F63B78u : crc >> 1;
+    }
+    return ~crc;
+}

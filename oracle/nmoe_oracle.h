@@ -132,6 +132,11 @@ uint32_t orc_lm_head_argmax(int dtype, const void *w, const uint16_t *s, const u
                             size_t in_dim, const float *x, const uint16_t *norm_w, float eps, int add_one,
                             float *logits);
 
+/* CRC-32C (Castagnoli, reflected 0x82F63B78, init/final xor 0xFFFFFFFF), bit at a time:
+ * the definition, for checking the library's table / SSE4.2 / device versions. Continues
+ * from `crc` (0 to start). */
+uint32_t orc_crc32c(uint32_t crc, const uint8_t *data, size_t n);
+
 /* Set the OpenMP thread count used by the matvecs (0 = library default). */
 void orc_set_threads(int n);
 int orc_get_threads(void);

@@ -88,6 +88,8 @@ def lib() -> C.CDLL:
         L.orc_lm_head_argmax.restype = C.c_uint32
         L.orc_lm_head_argmax.argtypes = [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_size_t,
                                          _f32p, C.c_void_p, C.c_float, C.c_int, C.c_void_p]
+        L.orc_crc32c.restype = C.c_uint32
+        L.orc_crc32c.argtypes = [C.c_uint32, C.c_void_p, C.c_size_t]
         L.orc_set_threads.argtypes = [C.c_int]
         L.orc_get_threads.restype = C.c_int
         _lib = L
@@ -330,3 +332,9 @@ def lm_head_argmax(head: LmHead, x: np.ndarray, norm_w: np.ndarray | None = None
                                    head.vocab, HIDDEN, x, None if nw is None else nw.ctypes.data, eps,
                                    int(add_one), logits.ctypes.data)
     return int(tok), logits
+
+
+def crc32c(data, crc: int = 0) -> int:
+    """CRC-32C of a bytes-like / numpy buffer (bitwise definition)."""
+    a = np.ascontiguousarray(np.frombuffer(data, np.uint8) if isinstance(data, (bytes, bytearray)) else data).view(np.uint8)
+    return int(lib().orc_crc32c(crc, a.ctypes.data, a.nbytes))
