@@ -103,9 +103,10 @@ struct GemmParams {
 };
 
 // Trace rows (1024 entries each): 0 producer slot acquired, 1 B stage issued, 2 dequant
-// step start, 3 dequant step end, 4 MMA step issued, 5 epilogue item start, 6 item end,
-// 7 raw slot data landed, 8 MMA step B ready, 9 dequant step end (last warp), 10 dequant
-// step begins waiting, 11 A stage free, 12 scales ready.
+// step start, 3 dequant step end, 4 MMA step committed (matrix 0 issuer), 5 epilogue item
+// start, 6 item end, 7 raw slot data landed, 8 MMA step's A and B ready, 9 SwiGLU epilogue
+// chunk before / after its TMEM loads, 10 dequant step begins waiting, 11 A stage free,
+// 12 scales ready.
 constexpr int kTraceRow = 1024;
 constexpr int kTraceRows = 13;
 __device__ __forceinline__ void trace_put(const GemmParams &P, int row, uint32_t i) {
@@ -195,6 +196,12 @@ __device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sy
 __device__ __forceinline__ void tc_ld8(uint32_t taddr, uint32_t *r) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t *r) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
                  : "r"(taddr)
                  : "memory");
 }
@@ -465,9 +472,10 @@ struct GemmSmem {
     GemmTables T;
 };
 
+constexpr int kGemmEpiStage = 4 * 32 * 64;   // SwiGLU epilogue: 4 warps x 32 tokens x 32 bf16
 __host__ __device__ constexpr size_t gemm_smem_bytes(int sr) {
     return 1024 + (size_t)kGemmSB * kGemmBStage + (size_t)2 * kGemmSS * 2 * kGemmScStage +
-           (size_t)sr * kGemmSlot + sizeof(GemmSmem);
+           (size_t)sr * kGemmSlot + kGemmEpiStage + sizeof(GemmSmem);
 }
 
 // Position in a ring of mbarrier-guarded stages: index, phase parity, total advances.
@@ -639,7 +647,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
     uint8_t *sB = sm;                                  // kGemmSB x 16 KB
     uint8_t *sSc = sB + kGemmSB * kGemmBStage;         // 2 groups x kGemmSS x 2 x 4 KB
     uint8_t *sRaw = sSc + 2 * kGemmSS * 2 * kGemmScStage;  // sr x 8 KB
-    GemmSmem *S = reinterpret_cast<GemmSmem *>(sRaw + P.sr * kGemmSlot);
+    uint8_t *sEpi = sRaw + P.sr * kGemmSlot;               // kGemmEpiStage
+    GemmSmem *S = reinterpret_cast<GemmSmem *>(sEpi + kGemmEpiStage);
     const int SR = P.sr;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -782,6 +791,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
                     // a_full: the A rows are in TMEM and the B tile has landed
                     if (!mbar_wait_sleep(&S->a_full[a.idx], a.phase, deadline)) { ok = false; break; }
                     tc_fence_after();
+                    if (mat == 0) trace_put(P, 8, a.count);
                     if (mine) {
                         const uint64_t bd = sw128_desc(smem_u32(sB + a.idx * kGemmBStage));
                         const uint32_t a0 = tmem + kGemmAccCols + a.idx * kGemmACols + mat * 32;
@@ -790,6 +800,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
                         issued = true;
                     }
                     tc_commit(&S->a_empty[a.idx]);   // frees the A and the B stage
+                    if (mat == 0) trace_put(P, 4, a.count);
                     a.next();
                 }
                 if (!ok) break;
@@ -874,23 +885,56 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
             const int m = w.mt * 128 + row;
             const uint32_t tbase = tmem + ((uint32_t)(32 * eq) << 16) + ab * 128;
             const int obase = pr.out_base + w.sp * pr.split_rows + w.pos0;
-            for (int c0 = 0; c0 < w.n; c0 += 8) {
+            if (pr.epi == kEpiSwiGLU) {
+                // 32 tokens a round: one wait per 64 columns read (gate and up). SiLU(g) * u
+                // with the hardware exponential and reciprocal (a few ulp of fp32; the result
+                // is rounded to bf16): one epilogue warp per sub-partition runs this for every
+                // token, and the IEEE division and expf (tens of instructions each) had made
+                // the epilogue as long as the item's main loop. All 32 values are computed
+                // before any store, with no branch between them, so their latencies overlap.
+                uint16_t *o = static_cast<uint16_t *>(pr.out);
+                const int cbase = w.mt * 128 + 32 * eq;           // the warp's 32 act columns
+                const int lcol = kperm_pos(m) - cbase;            // this lane's, K-permuted
+                for (int c0 = 0; c0 < w.n; c0 += 32) {
+                    uint32_t g[32], u[32];
+                    if (tid == 384) trace_put(P, 9, 8 * tile + 2 * (c0 >> 5));
+                    tc_ld32(tbase + c0, g);
+                    tc_ld32(tbase + 128 + c0, u);
+                    tc_wait_ld();
+                    if (tid == 384) trace_put(P, 9, 8 * tile + 2 * (c0 >> 5) + 1);
+                    const int nc = min(32, w.n - c0);
+                    uint32_t av[16];
+#pragma unroll
+                    for (int jj = 0; jj < 32; jj += 2) {
+                        const float g0 = __uint_as_float(g[jj]), u0 = __uint_as_float(u[jj]);
+                        const float g1 = __uint_as_float(g[jj + 1]), u1 = __uint_as_float(u[jj + 1]);
+                        av[jj / 2] = pack_bf16x2(__fdividef(g0, 1.f + __expf(-g0)) * u0,
+                                                 __fdividef(g1, 1.f + __expf(-g1)) * u1);
+                    }
+                    // through shared memory, so that each store is 16 bytes of one token's
+                    // row instead of 2 bytes: the warp's [32 tokens][32 columns] tile
+                    uint16_t *tile16 = reinterpret_cast<uint16_t *>(sEpi + eq * 2048);
+#pragma unroll
+                    for (int jj = 0; jj < 32; ++jj) tile16[jj * 32 + lcol] = (uint16_t)(av[jj / 2] >> (16 * (jj & 1)));
+                    __syncwarp();
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int q = lane + 32 * i, tk = q >> 2, part = q & 3;
+                        if (tk < nc) {
+                            const uint4 v = *reinterpret_cast<const uint4 *>(tile16 + tk * 32 + part * 8);
+                            *reinterpret_cast<uint4 *>(o + (size_t)(obase + c0 + tk) * pr.ld_out + cbase + part * 8) = v;
+                        }
+                    }
+                    __syncwarp();
+                }
+            }
+            for (int c0 = 0; pr.epi != kEpiSwiGLU && c0 < w.n; c0 += 8) {
                 uint32_t g[8], u[8];
                 tc_ld8(tbase + c0, g);
                 if (pr.n_mat == 2) tc_ld8(tbase + 128 + c0, u);
                 tc_wait_ld();
                 const int nc = min(8, w.n - c0);
-                if (pr.epi == kEpiSwiGLU) {
-                    uint16_t *o = static_cast<uint16_t *>(pr.out);
-                    const int col = kperm_pos(m);
-#pragma unroll
-                    for (int jj = 0; jj < 8; ++jj)
-                        if (jj < nc) {
-                            const float gv = __uint_as_float(g[jj]), uv = __uint_as_float(u[jj]);
-                            const float a = gv / (1.f + expf(-gv)) * uv;
-                            o[(size_t)(obase + c0 + jj) * pr.ld_out + col] = (uint16_t)(pack_bf16x2(a, 0.f) & 0xFFFFu);
-                        }
-                } else if (pr.epi == kEpiBf16) {
+                if (pr.epi == kEpiBf16) {
                     uint16_t *o = static_cast<uint16_t *>(pr.out);
 #pragma unroll
                     for (int jj = 0; jj < 8; ++jj)
