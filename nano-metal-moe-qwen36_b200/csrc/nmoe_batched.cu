@@ -78,6 +78,7 @@ struct BatchedState {
 // after that peer returned this rank's rows of the call two back, so nothing overwrites
 // data still being read.
 constexpr int kEpMaxWorld = 8;
+static_assert(kEpMaxWorld <= kGemmMaxPeers, "GEMM return pointers per rank");
 struct EpLayout {              // offsets inside each rank's arena
     size_t flags;              // arrive[kEpMaxWorld], ret[kEpMaxWorld]: u32, 64 bytes apart
     size_t rcnt;               // [2][W][n_local] int: rows per (source, local expert)
@@ -95,6 +96,8 @@ struct EpState {
     uint8_t *peer[kEpMaxWorld] = {};   // every rank's arena as mapped here (peer[rank] = arena)
     uint8_t **d_peer = nullptr;  // device copy of peer[]
     uint16_t *yr = nullptr;      // [W * C][2048] down outputs of the received rows (slab order)
+    int return_kernel = 0;       // NMOE_EP_RETURN_KERNEL=1: a separate return kernel instead of
+                                 // the down epilogue's peer stores
     unsigned *done = nullptr;    // [2] grid completion counters (dispatch, return)
     uint32_t call = 0;           // calls so far; the tag of a call is call + 1
     bool timing = false;         // NMOE_EP_TIMING=1: events around the exchanges
@@ -418,6 +421,16 @@ __global__ void __launch_bounds__(256) k_ep_dispatch(EpArgs a, const uint16_t *x
         if (tid == 0) reinterpret_cast<int *>(a.peer[b] + a.L.rmeta)[a.set * a.world + a.rank] = eoff[b * nl];
     }
     ep_signal_last(a, 0, a.done);
+}
+
+// Raise this rank's flag `which` in every arena (one block; the stores it announces were
+// made by earlier kernels on the stream, each fenced system-wide by its writer).
+__global__ void k_ep_signal(EpArgs a, int which) {
+    __threadfence_system();
+    const int p = threadIdx.x;
+    if (p < a.world)
+        st_release_sys_u32(reinterpret_cast<uint32_t *>(a.peer[p] + a.L.flags) + (which * kEpMaxWorld + a.rank) * 16,
+                           a.tag);
 }
 
 // Wait (bounded) until every rank's flag `which` in this rank's arena carries the tag.
@@ -749,6 +762,7 @@ int nmoe_batched_init(nmoe_moe_ctx *ctx) {
             return NMOE_ECUDA;
         }
         if (const char *t = getenv("NMOE_EP_TIMING")) E->timing = atoi(t) != 0;
+        if (const char *t = getenv("NMOE_EP_RETURN_KERNEL")) E->return_kernel = atoi(t) != 0;
         if (E->timing)
             for (auto &ev : E->ev) cudaEventCreate(&ev);
         // every rank has mapped every arena before any rank's first dispatch writes into one
@@ -1067,6 +1081,12 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
         r.epi = kEpiBf16;
         r.ld_out = kHidden;
         r.out = E ? E->yr : B->y;
+        if (E != nullptr && !E->return_kernel) {
+            // the down epilogue writes each output row into its source's return buffer
+            r.ret_meta = reinterpret_cast<const int *>(E->arena + E->L.rmeta) + (size_t)ea.set * E->world;
+            for (int p = 0; p < E->world; ++p)
+                r.ret_base[p] = E->peer[p] + E->L.yret + (size_t)ea.set * E->C * kHidden * 2;
+        }
         bool ok = make_cm_maps(B, r, experts + pg.gu_bytes, pg, ctx->n_local);
         GemmProblem &s = P.prob[1];
         s.fmt = sfmt;
@@ -1102,7 +1122,8 @@ extern "C" int nmoe_moe_forward_batched(nmoe_moe_ctx *ctx, int layer, int T, int
     const uint16_t *ysrc = B->y;
     if (E != nullptr) {
         if (E->timing) cudaEventRecord(E->ev[2], st);
-        k_ep_return<<<16 * ctx->num_sms, 256, 0, st>>>(ea, E->yr);
+        if (E->return_kernel) k_ep_return<<<16 * ctx->num_sms, 256, 0, st>>>(ea, E->yr);
+        else k_ep_signal<<<1, 32, 0, st>>>(ea, 1);   // the down epilogue already wrote the rows
         k_ep_wait<<<1, 32, 0, st>>>(ea, 1, ctx->d_err, B->timeout_ns);
         if (E->timing) cudaEventRecord(E->ev[3], st);
         if ((e = cudaGetLastError()) != cudaSuccess) {

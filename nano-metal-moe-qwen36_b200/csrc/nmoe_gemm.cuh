@@ -45,6 +45,7 @@ constexpr int kGemmThreads = 512;
 constexpr int kGemmNChunk = 128;       // tokens per item (MMA N <= 128)
 constexpr int kGemmMaxGroups = 256;
 constexpr int kGemmMaxProblems = 2;
+constexpr int kGemmMaxPeers = 8;       // expert parallelism: ranks whose return buffers an epilogue writes
 constexpr int kGemmSA = 4, kGemmSB = kGemmSA, kGemmSS = 2;   // kGemmSS scale stages per dequant group
 // A step's A stage (TMEM) and B stage (shared memory) share one ring position: one MMA
 // commit frees both, and the B tile's TMA completes on the stage's a_full barrier, so the
@@ -90,6 +91,11 @@ struct alignas(64) GemmProblem {
     int ld_out;
     int mat_col;              // kEpiF32 with two matrices: column offset of the second
     void *out;
+    // expert parallelism, kEpiBf16: the rows of slab r go straight to rank r's return
+    // buffer ret_base[r] (peer memory over NVLink), at row ret_meta[r] + (position -
+    // r * slab_rows); nullptr: rows go to `out`
+    const int *ret_meta;
+    uint8_t *ret_base[kGemmMaxPeers];
 };
 
 struct GemmParams {
@@ -928,35 +934,63 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_moe_gemm(const __grid_const
                     __syncwarp();
                 }
             }
-            for (int c0 = 0; pr.epi != kEpiSwiGLU && c0 < w.n; c0 += 8) {
+            if (pr.epi == kEpiBf16) {
+                // 32 tokens a round through shared memory: 16-byte stores of one token's row
+                // (a peer's memory under expert parallelism: 2-byte stores over NVLink were
+                // the slow part of an earlier version)
+                const int cbase = w.mt * 128 + 32 * eq;
+                uint16_t *dst0;
+                if (pr.ret_meta != nullptr) {
+                    const int r = w.g / pr.slab_groups;
+                    dst0 = reinterpret_cast<uint16_t *>(pr.ret_base[r]) +
+                           (size_t)(pr.ret_meta[r] + w.pos0 - r * pr.slab_rows) * pr.ld_out;
+                } else {
+                    dst0 = static_cast<uint16_t *>(pr.out) + (size_t)obase * pr.ld_out;
+                }
+                uint16_t *tile16 = reinterpret_cast<uint16_t *>(sEpi + eq * 2048);
+                for (int c0 = 0; c0 < w.n; c0 += 32) {
+                    uint32_t g[32];
+                    tc_ld32(tbase + c0, g);
+                    tc_wait_ld();
+                    const int nc = min(32, w.n - c0);
+#pragma unroll
+                    for (int jj = 0; jj < 32; ++jj)
+                        tile16[jj * 32 + lane] = (uint16_t)(pack_bf16x2(__uint_as_float(g[jj]), 0.f) & 0xFFFFu);
+                    __syncwarp();
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int q = lane + 32 * i, tk = q >> 2, part = q & 3;
+                        if (tk < nc) {
+                            const uint4 v = *reinterpret_cast<const uint4 *>(tile16 + tk * 32 + part * 8);
+                            *reinterpret_cast<uint4 *>(dst0 + (size_t)(c0 + tk) * pr.ld_out + cbase + part * 8) = v;
+                        }
+                    }
+                    __syncwarp();
+                }
+            }
+            for (int c0 = 0; pr.epi == kEpiF32 && c0 < w.n; c0 += 8) {
                 uint32_t g[8], u[8];
                 tc_ld8(tbase + c0, g);
                 if (pr.n_mat == 2) tc_ld8(tbase + 128 + c0, u);
                 tc_wait_ld();
                 const int nc = min(8, w.n - c0);
-                if (pr.epi == kEpiBf16) {
-                    uint16_t *o = static_cast<uint16_t *>(pr.out);
+                float *o = static_cast<float *>(pr.out);
 #pragma unroll
-                    for (int jj = 0; jj < 8; ++jj)
-                        if (jj < nc)
-                            o[(size_t)(obase + c0 + jj) * pr.ld_out + m] =
-                                (uint16_t)(pack_bf16x2(__uint_as_float(g[jj]), 0.f) & 0xFFFFu);
-                } else {
-                    float *o = static_cast<float *>(pr.out);
-#pragma unroll
-                    for (int jj = 0; jj < 8; ++jj)
-                        if (jj < nc) {
-                            o[(size_t)(obase + c0 + jj) * pr.ld_out + m] = __uint_as_float(g[jj]);
-                            if (pr.n_mat == 2)
-                                o[(size_t)(obase + c0 + jj) * pr.ld_out + pr.mat_col + m] = __uint_as_float(u[jj]);
-                        }
-                }
+                for (int jj = 0; jj < 8; ++jj)
+                    if (jj < nc) {
+                        o[(size_t)(obase + c0 + jj) * pr.ld_out + m] = __uint_as_float(g[jj]);
+                        if (pr.n_mat == 2)
+                            o[(size_t)(obase + c0 + jj) * pr.ld_out + pr.mat_col + m] = __uint_as_float(u[jj]);
+                    }
             }
             tc_fence_before();
             __syncwarp();
             if (tid == 384) trace_put(P, 6, tile);
             if (lane == 0) mbar_arrive(&S->acc_empty[ab]);
         }
+        // rows written to peers' return buffers: visible system-wide before the kernel
+        // ends (the signal kernel that follows announces them)
+        if (P.prob[0].ret_meta != nullptr) __threadfence_system();
     }
 
     tc_fence_before();
