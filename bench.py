@@ -673,6 +673,7 @@ def run_ours(args, rank, world, local_rank):
     if args.lm_head and rank == 0:
         result["lm_head"] = run_lm_head(args, dev)
         result["layer_crc32c"] = run_crc(args, dev)
+        result["linear_attn"] = run_linear_attn(args, dev)
     if args.ep_tokens > 0:
         ep = run_ep_batched(args, rank, world, dev)
         if result is not None:
@@ -799,6 +800,67 @@ def run_crc(args, dev):
             "note": "load-time integrity check (nmoe_moe_load_layer_checked), not on the decode path"}
 
 
+def linear_attn_bytes() -> int:
+    """Algorithmic bytes of one linear-attention step: the recurrent state read and written
+    (32 x 128 x 128 f32), the conv state read and written, conv weights, qkv, z, out, and the
+    per-head vectors."""
+    state = 32 * 128 * 128 * 4
+    conv = 3 * 8192 * 4
+    return 2 * state + 2 * conv + 8192 * 4 * 2 + 8192 * 4 + 4096 * 4 * 2 + 32 * 4 * 3 + 32 * 2 + 128 * 2
+
+
+def run_linear_attn(args, dev):
+    """GatedDeltaNet decode-step core (nmoe_linear_attn_step) over 64 layers' states (134 MB,
+    above L2): device time per call against the HBM roofline, and the oracle on the host."""
+    import torch
+    import nmoe_b200 as N
+    from oracle import oracle as O
+    L = 64
+    w = O.make_linear_attn(args.seed + 11)
+    dw = {k: torch.from_numpy(v.view(np.int16) if v.dtype == np.uint16 else v).to(f"cuda:{dev}") for k, v in w.items()}
+    rng = np.random.default_rng(args.seed + 12)
+    inp = O.linear_attn_inputs(rng)
+    di = {k: torch.from_numpy(v).to(f"cuda:{dev}") for k, v in inp.items()}
+    conv = torch.zeros((L, 3, 8192), device=f"cuda:{dev}")
+    S = torch.zeros((L, 32, 128, 128), device=f"cuda:{dev}")
+    out = torch.zeros(4096, device=f"cuda:{dev}")
+    st = torch.cuda.Stream(device=dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=st):
+        for l in range(L):
+            N.linear_attn_step(dw, di["qkv"], di["z"], di["alpha"], di["beta"], conv[l], S[l], out,
+                               stream=torch.cuda.current_stream().cuda_stream)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    reps = 20
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    with torch.cuda.stream(st):
+        for _ in range(reps):
+            g.replay()
+    e1.record(st)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * L)
+    hc, hs = np.zeros((3, 8192), np.float32), np.zeros((32, 128, 128), np.float32)
+    t0 = time.perf_counter()
+    n = 0
+    while time.perf_counter() - t0 < 1.0:
+        O.linear_attn_step(w, inp, hc, hs)
+        n += 1
+    cpu_us = (time.perf_counter() - t0) / n * 1e6
+    ab = linear_attn_bytes()
+    pk, pk_kind = peaks()
+    ach = ab / (us * 1e-6) / 1e9
+    return {"us_per_call": us, "calls_per_s": 1e6 / us,
+            "roofline": {"bound": "hbm", "achieved": ach, "peak": pk, "unit": "GB/s", "frac": ach / pk,
+                         "peak_kind": pk_kind, "algorithmic_bytes_per_launch": ab},
+            "cpu_oracle_us_per_call": cpu_us, "cpu_oracle_threads": 1,
+            "config": {"layers_cycled": L, "state_bytes": L * (32 * 128 * 128 + 3 * 8192) * 4,
+                       "timing": "CUDA graph of 64 calls (one per layer state) x 20 replays, CUDA events; "
+                                 "states above L2"}}
+
+
 def run_ep_batched(args, rank, world, dev):
     """Config 2 beside the decode line, at every N: T tokens per rank (--ep-tokens) through
     --ep-layers resident layers per step, experts sharded 256/N per GPU with token rows
@@ -876,7 +938,7 @@ def main():
     ap.add_argument("--pool", type=int, default=32, help="distinct expert packs generated on the host")
     ap.add_argument("--seed", type=int, default=2026)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--workload", choices=["decode", "batched", "lm_head", "crc"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "batched", "lm_head", "crc", "linear_attn"], default="decode")
     ap.add_argument("--lm-dtypes", default="q4,bf16", help="LM head weight types timed (q4, bf16)")
     ap.add_argument("--bits", type=int, choices=[2, 4], default=4, help="decode: expert packs (4: config 0, 2: config 1)")
     ap.add_argument("--k", type=int, default=8, help="decode: routed experts per token (config 1 sweeps 1..8)")
@@ -909,7 +971,11 @@ def main():
         import torch.distributed as dist
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local_rank}"))
-    if args.workload == "crc":
+    if args.workload == "linear_attn":
+        import torch
+        torch.cuda.set_device(local_rank)
+        res = {"workload": "linear_attn", **run_linear_attn(args, local_rank)} if rank == 0 else None
+    elif args.workload == "crc":
         import torch
         torch.cuda.set_device(local_rank)
         res = {"workload": "crc", **run_crc(args, local_rank)} if rank == 0 else None

@@ -299,6 +299,26 @@ int nmoe_lm_head_argmax(const nmoe_tensor *head, int head_dtype, int vocab, int 
 size_t nmoe_lm_head_workspace_bytes(void);
 const char *nmoe_lm_head_error(void);
 
+/* ---- Linear attention (GatedDeltaNet) core of one decode step ---------------------
+ * Replaces the five kernels of NMOELinearAttentionStepMetal between the fused
+ * qkv/z/beta/alpha projection and the output projection (src/runtime.m:3390-3478):
+ * conv1d step, per-head q/k RMS norm, decay/beta, the gated delta rule on the recurrent
+ * state, and the z-gated RMS norm (metal/kernels.metal:1275-1346, 1780-1873). Qwen3.6
+ * geometry: 16 key heads and 32 value heads of 128, conv width 4 over 8192 channels.
+ * All pointers are DEVICE memory: qkv f32[8192] (q 0..2047, k 2048..4095, v 4096..8191),
+ * z f32[4096], alpha f32[32], beta f32[32]; conv_state f32[3][8192] and delta_state
+ * f32[32][128][128] (16-byte aligned) are updated in place; out f32[4096] feeds the output
+ * projection. One launch of 16 clusters x 8 CTAs; allocates nothing; capturable. */
+typedef struct nmoe_linear_attn_weights {
+    const uint16_t *conv_w;   /* bf16 [8192][4]  linear_attn.conv1d.weight (8-byte aligned) */
+    const float *A_log;       /* f32 [32]        linear_attn.A_log                          */
+    const uint16_t *dt_bias;  /* bf16 [32]       linear_attn.dt_bias                        */
+    const uint16_t *norm_w;   /* bf16 [128]      linear_attn.norm.weight                    */
+} nmoe_linear_attn_weights;
+int nmoe_linear_attn_step(const nmoe_linear_attn_weights *w, const float *qkv, const float *z,
+                          const float *alpha, const float *beta, float *conv_state, float *delta_state,
+                          float *out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

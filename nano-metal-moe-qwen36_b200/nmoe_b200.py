@@ -33,7 +33,7 @@ ABI_SYMBOLS = (
     "nmoe_moe_static_scratch_bytes", "nmoe_moe_static_status", "nmoe_moe_debug_ep_times",
     "nmoe_lm_head_argmax", "nmoe_lm_head_workspace_bytes", "nmoe_lm_head_error",
     "nmoe_moe_load_layer_checked", "nmoe_moe_load_layer_file_checked", "nmoe_crc32c", "nmoe_crc32c_combine",
-    "nmoe_crc32c_device",
+    "nmoe_crc32c_device", "nmoe_linear_attn_step",
 )
 
 
@@ -59,6 +59,10 @@ class Tensor(C.Structure):
 class DenseWeights(C.Structure):
     _fields_ = [("router", Tensor), ("shared_gate", Tensor), ("shared_up", Tensor),
                 ("shared_down", Tensor), ("shared_gate_vec", Tensor)]
+
+
+class LinearAttnWeights(C.Structure):
+    _fields_ = [("conv_w", C.c_void_p), ("A_log", C.c_void_p), ("dt_bias", C.c_void_p), ("norm_w", C.c_void_p)]
 
 
 def build(quiet: bool = True) -> str:
@@ -137,6 +141,8 @@ def lib() -> C.CDLL:
     L.nmoe_crc32c_device.argtypes = [vp, sz, i, vp, vp]
     L.nmoe_crc32c_combine.restype = C.c_uint32
     L.nmoe_crc32c_combine.argtypes = [C.c_uint32, C.c_uint32, sz]
+    L.nmoe_linear_attn_step.restype = i
+    L.nmoe_linear_attn_step.argtypes = [C.POINTER(LinearAttnWeights), vp, vp, vp, vp, vp, vp, vp, vp]
     L.nmoe_lm_head_argmax.restype = i
     L.nmoe_lm_head_argmax.argtypes = [C.POINTER(Tensor), i, i, i, vp, i, vp, C.c_float, i, vp, vp, vp, vp]
     L.nmoe_lm_head_workspace_bytes.restype = sz
@@ -435,3 +441,14 @@ def crc32c_device(data, blob_bytes: int, nblobs: int, out, stream=0):
     rc = lib().nmoe_crc32c_device(_ptr(data), blob_bytes, nblobs, _ptr(out), stream)
     if rc != OK:
         raise NmoeError(rc, "nmoe_crc32c_device")
+
+
+def linear_attn_step(weights: dict, qkv, z, alpha, beta, conv_state, delta_state, out, stream=0):
+    """nmoe_linear_attn_step: GatedDeltaNet core of one decode step (device tensors);
+    `weights` = {"conv_w", "A_log", "dt_bias", "norm_w"}. States are updated in place."""
+    w = LinearAttnWeights(_ptr(weights["conv_w"]), _ptr(weights["A_log"]), _ptr(weights["dt_bias"]),
+                          _ptr(weights["norm_w"]))
+    rc = lib().nmoe_linear_attn_step(C.byref(w), _ptr(qkv), _ptr(z), _ptr(alpha), _ptr(beta), _ptr(conv_state),
+                                     _ptr(delta_state), _ptr(out), stream)
+    if rc != OK:
+        raise NmoeError(rc, "nmoe_linear_attn_step")

@@ -509,3 +509,74 @@ uint32_t orc_crc32c(uint32_t crc, const uint8_t *data, size_t n) {
     }
     return ~crc;
 }
+
+/* ------------------------------------------------- linear attention step ---- */
+
+#define ORC_LA_KH 16
+#define ORC_LA_VH 32
+#define ORC_LA_D 128
+#define ORC_LA_CONV 8192
+
+void orc_linear_attn_step(const float *qkv, const float *z, const float *alpha, const float *beta,
+                          const uint16_t *conv_w, const float *A_log, const uint16_t *dt_bias,
+                          const uint16_t *norm_w, float *conv_state, float *delta_state, float *out) {
+    float *cv = (float *)malloc(ORC_LA_CONV * sizeof(float));
+    /* kernels.metal:1275-1295 */
+    for (int i = 0; i < ORC_LA_CONV; i++) {
+        float acc = 0.0f;
+        acc += conv_state[0 * ORC_LA_CONV + i] * orc_bf16_to_f32(conv_w[4 * i + 0]);
+        acc += conv_state[1 * ORC_LA_CONV + i] * orc_bf16_to_f32(conv_w[4 * i + 1]);
+        acc += conv_state[2 * ORC_LA_CONV + i] * orc_bf16_to_f32(conv_w[4 * i + 2]);
+        const float inp = qkv[i];
+        acc += inp * orc_bf16_to_f32(conv_w[4 * i + 3]);
+        cv[i] = orc_silu_kernel(acc);
+        conv_state[0 * ORC_LA_CONV + i] = conv_state[1 * ORC_LA_CONV + i];
+        conv_state[1 * ORC_LA_CONV + i] = conv_state[2 * ORC_LA_CONV + i];
+        conv_state[2 * ORC_LA_CONV + i] = inp;
+    }
+    /* kernels.metal:1780-1821, inv_scale = 1/sqrt(128), eps 1e-12 (src/runtime.m:3360, 3410) */
+    const float inv_scale = 1.0f / sqrtf((float)ORC_LA_D);
+    for (int h = 0; h < ORC_LA_KH; h++) {
+        float *q = cv + h * ORC_LA_D, *k = cv + 2048 + h * ORC_LA_D;
+        float sq = 0.0f, sk = 0.0f;
+        for (int i = 0; i < ORC_LA_D; i++) sq += q[i] * q[i];
+        const float qi = 1.0f / sqrtf(sq / (float)ORC_LA_D + 1e-12f);
+        for (int i = 0; i < ORC_LA_D; i++) q[i] = q[i] * qi * inv_scale * inv_scale;
+        for (int i = 0; i < ORC_LA_D; i++) sk += k[i] * k[i];
+        const float ki = 1.0f / sqrtf(sk / (float)ORC_LA_D + 1e-12f);
+        for (int i = 0; i < ORC_LA_D; i++) k[i] = k[i] * ki * inv_scale;
+    }
+    for (int vh = 0; vh < ORC_LA_VH; vh++) {
+        /* kernels.metal:1823-1839 */
+        const float A = expf(A_log[vh]);
+        const float sp = logf(1.0f + expf(alpha[vh] + orc_bf16_to_f32(dt_bias[vh])));
+        const float g = expf(-A * sp);
+        const float b = orc_sigmoid_kernel(beta[vh]);
+        const int kh = vh / 2;
+        const float *q = cv + kh * ORC_LA_D, *k = cv + 2048 + kh * ORC_LA_D, *v = cv + 4096 + vh * ORC_LA_D;
+        float o[ORC_LA_D];
+        /* kernels.metal:1300-1346 */
+        for (int vi = 0; vi < ORC_LA_D; vi++) {
+            float *S = delta_state + ((size_t)vh * ORC_LA_D + vi) * ORC_LA_D;
+            float kv = 0.0f;
+            for (int i = 0; i < ORC_LA_D; i++) {
+                const float s = S[i] * g;
+                S[i] = s;
+                kv += s * k[i];
+            }
+            const float d = (v[vi] - kv) * b;
+            for (int i = 0; i < ORC_LA_D; i++) S[i] += k[i] * d;
+            float ov = 0.0f;
+            for (int i = 0; i < ORC_LA_D; i++) ov += S[i] * q[i];
+            o[vi] = ov;
+        }
+        /* kernels.metal:1841-1873, eps 1e-6 */
+        float ss = 0.0f;
+        for (int vi = 0; vi < ORC_LA_D; vi++) ss += o[vi] * o[vi];
+        const float inv = 1.0f / sqrtf(ss / (float)ORC_LA_D + 1e-6f);
+        for (int vi = 0; vi < ORC_LA_D; vi++)
+            out[vh * ORC_LA_D + vi] = o[vi] * inv * orc_silu_kernel(z[vh * ORC_LA_D + vi]) *
+                                      orc_bf16_to_f32(norm_w[vi]);
+    }
+    free(cv);
+}

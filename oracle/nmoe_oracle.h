@@ -137,6 +137,25 @@ uint32_t orc_lm_head_argmax(int dtype, const void *w, const uint16_t *s, const u
  * from `crc` (0 to start). */
 uint32_t orc_crc32c(uint32_t crc, const uint8_t *data, size_t n);
 
+/* Linear-attention (GatedDeltaNet) core of one decode step, Qwen3.6 geometry: 16 key heads
+ * x 128, 32 value heads x 128, conv width 4 over 8192 channels (q 0..2047, k 2048..4095,
+ * v 4096..8191). The reference's sequence (src/runtime.m:3390-3478):
+ *   nmoe_conv1d_step      (metal/kernels.metal:1275-1295): out = SiLU(sum of 4 taps),
+ *                          conv_state shifted, the input appended;
+ *   nmoe_rms_norm_qk      (kernels.metal:1780-1821): per key head, q * rsqrt(mean q^2 + 1e-12)
+ *                          / key_dim, k * rsqrt(mean k^2 + 1e-12) / sqrt(key_dim);
+ *   nmoe_compute_decay_beta (kernels.metal:1823-1839): g = exp(-exp(A_log) softplus(alpha +
+ *                          dt_bias)), b = sigmoid(beta);
+ *   nmoe_gated_delta_net_step (kernels.metal:1300-1346): S = g S; d = (v - S k) b; S += k d;
+ *                          o = S q (value head vh reads key head vh / 2);
+ *   nmoe_gated_rms_norm    (kernels.metal:1841-1873): o * rsqrt(mean o^2 + 1e-6) * SiLU(z) * w.
+ * qkv[8192], z[4096], alpha[32], beta[32]; conv_w bf16 [8192][4], A_log f32[32], dt_bias
+ * bf16[32], norm_w bf16[128]; conv_state f32 [3][8192] and delta_state f32 [32][128][128]
+ * are updated in place; out[4096]. Sums run in the reference kernels' sequential order. */
+void orc_linear_attn_step(const float *qkv, const float *z, const float *alpha, const float *beta,
+                          const uint16_t *conv_w, const float *A_log, const uint16_t *dt_bias,
+                          const uint16_t *norm_w, float *conv_state, float *delta_state, float *out);
+
 /* Set the OpenMP thread count used by the matvecs (0 = library default). */
 void orc_set_threads(int n);
 int orc_get_threads(void);

@@ -90,6 +90,8 @@ def lib() -> C.CDLL:
                                          _f32p, C.c_void_p, C.c_float, C.c_int, C.c_void_p]
         L.orc_crc32c.restype = C.c_uint32
         L.orc_crc32c.argtypes = [C.c_uint32, C.c_void_p, C.c_size_t]
+        L.orc_linear_attn_step.argtypes = [_f32p, _f32p, _f32p, _f32p, _u16p, _f32p, _u16p, _u16p, _f32p, _f32p,
+                                           _f32p]
         L.orc_set_threads.argtypes = [C.c_int]
         L.orc_get_threads.restype = C.c_int
         _lib = L
@@ -338,3 +340,31 @@ def crc32c(data, crc: int = 0) -> int:
     """CRC-32C of a bytes-like / numpy buffer (bitwise definition)."""
     a = np.ascontiguousarray(np.frombuffer(data, np.uint8) if isinstance(data, (bytes, bytearray)) else data).view(np.uint8)
     return int(lib().orc_crc32c(crc, a.ctypes.data, a.nbytes))
+
+
+# ------------------------------------------------------- linear attention ----
+
+def make_linear_attn(seed: int):
+    """Seeded linear-attention weights and step inputs at Qwen3.6 geometry."""
+    rng = np.random.default_rng(seed)
+    w = {"conv_w": randn_bf16(rng, (8192, 4), 0.3),
+         "A_log": (rng.standard_normal(32) * 0.5).astype(np.float32),
+         "dt_bias": randn_bf16(rng, (32,), 0.5),
+         "norm_w": f32_to_bf16(1.0 + rng.standard_normal(128).astype(np.float32) * 0.1)}
+    return w
+
+
+def linear_attn_inputs(rng):
+    return {"qkv": rng.standard_normal(8192).astype(np.float32),
+            "z": rng.standard_normal(4096).astype(np.float32),
+            "alpha": rng.standard_normal(32).astype(np.float32),
+            "beta": rng.standard_normal(32).astype(np.float32)}
+
+
+def linear_attn_step(w, inp, conv_state, delta_state):
+    """One step by the reference kernels' sequence; states updated in place; returns out[4096]."""
+    out = np.zeros(4096, np.float32)
+    lib().orc_linear_attn_step(inp["qkv"], inp["z"], inp["alpha"], inp["beta"], w["conv_w"].reshape(-1),
+                               w["A_log"], w["dt_bias"], w["norm_w"], conv_state.reshape(-1),
+                               delta_state.reshape(-1), out)
+    return out
