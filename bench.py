@@ -674,6 +674,7 @@ def run_ours(args, rank, world, local_rank):
         result["lm_head"] = run_lm_head(args, dev)
         result["layer_crc32c"] = run_crc(args, dev)
         result["linear_attn"] = run_linear_attn(args, dev)
+        result["full_attn"] = run_full_attn(args, dev)
     if args.ep_tokens > 0:
         ep = run_ep_batched(args, rank, world, dev)
         if result is not None:
@@ -861,6 +862,60 @@ def run_linear_attn(args, dev):
                                  "states above L2"}}
 
 
+def run_full_attn(args, dev):
+    """Full-attention decode step (nmoe_full_attn_step) at positions 4095 and 32767: device
+    time per call (CUDA graph of 20 calls x 5 replays), bytes = the K and V rows read plus
+    the new rows written, against HBM; the oracle's time at position 4095 on one core."""
+    import torch
+    import nmoe_b200 as N
+    from oracle import oracle as O
+    rng = np.random.default_rng(args.seed + 21)
+    w = {"q_norm": O.randn_bf16(rng, (256,), 0.1), "k_norm": O.randn_bf16(rng, (256,), 0.1)}
+    dw = {k: torch.from_numpy(v.view(np.int16).copy()).to(f"cuda:{dev}") for k, v in w.items()}
+    ws = torch.zeros(N.full_attn_workspace_bytes() // 4, dtype=torch.int32, device=f"cuda:{dev}")
+    q = torch.randn(16, 512, device=f"cuda:{dev}")
+    kn = torch.randn(2, 256, device=f"cuda:{dev}")
+    vn = torch.randn(2, 256, device=f"cuda:{dev}")
+    out = torch.zeros(16 * 256, device=f"cuda:{dev}")
+    pk, pk_kind = peaks()
+    res = {}
+    st = torch.cuda.Stream(device=dev)
+    for pos in (4095, 32767):
+        cap = pos + 1
+        kc = torch.randn(cap, 2, 256, device=f"cuda:{dev}") * 0.3
+        vc = torch.randn(cap, 2, 256, device=f"cuda:{dev}")
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            for _ in range(20):
+                N.full_attn_step(dw, q, kn, vn, kc, vc, pos, cap, out, ws,
+                                 stream=torch.cuda.current_stream().cuda_stream)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        with torch.cuda.stream(st):
+            for _ in range(5):
+                g.replay()
+        e1.record(st)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / 100
+        ab = (pos + 1) * 2 * 256 * 4 * 2 + 16 * 512 * 4 + 16 * 256 * 4
+        ach = ab / (us * 1e-6) / 1e9
+        res[f"position_{pos}"] = {"us_per_call": us, "roofline": {"bound": "hbm", "achieved": ach, "peak": pk,
+                                  "unit": "GB/s", "frac": ach / pk, "peak_kind": pk_kind,
+                                  "algorithmic_bytes_per_launch": ab},
+                                  "l2": "K and V of 32768 positions = 128 MB, about the L2 size"
+                                        if pos > 8192 else "16 MB of K and V: L2-resident across calls"}
+        del g, kc, vc
+    hk = np.zeros((4096, 2, 256), np.float32)
+    hv = np.zeros((4096, 2, 256), np.float32)
+    t0 = time.perf_counter()
+    O.full_attn_step(q.cpu().numpy(), kn.cpu().numpy(), vn.cpu().numpy(), w["q_norm"], w["k_norm"], hk, hv, 4095)
+    res["cpu_oracle_ms_at_4095"] = (time.perf_counter() - t0) * 1e3
+    return res
+
+
 def run_ep_batched(args, rank, world, dev):
     """Config 2 beside the decode line, at every N: T tokens per rank (--ep-tokens) through
     --ep-layers resident layers per step, experts sharded 256/N per GPU with token rows
@@ -938,7 +993,7 @@ def main():
     ap.add_argument("--pool", type=int, default=32, help="distinct expert packs generated on the host")
     ap.add_argument("--seed", type=int, default=2026)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--workload", choices=["decode", "batched", "lm_head", "crc", "linear_attn"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "batched", "lm_head", "crc", "linear_attn", "full_attn"], default="decode")
     ap.add_argument("--lm-dtypes", default="q4,bf16", help="LM head weight types timed (q4, bf16)")
     ap.add_argument("--bits", type=int, choices=[2, 4], default=4, help="decode: expert packs (4: config 0, 2: config 1)")
     ap.add_argument("--k", type=int, default=8, help="decode: routed experts per token (config 1 sweeps 1..8)")
@@ -971,7 +1026,11 @@ def main():
         import torch.distributed as dist
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local_rank}"))
-    if args.workload == "linear_attn":
+    if args.workload == "full_attn":
+        import torch
+        torch.cuda.set_device(local_rank)
+        res = {"workload": "full_attn", **run_full_attn(args, local_rank)} if rank == 0 else None
+    elif args.workload == "linear_attn":
         import torch
         torch.cuda.set_device(local_rank)
         res = {"workload": "linear_attn", **run_linear_attn(args, local_rank)} if rank == 0 else None

@@ -319,6 +319,27 @@ int nmoe_linear_attn_step(const nmoe_linear_attn_weights *w, const float *qkv, c
                           const float *alpha, const float *beta, float *conv_state, float *delta_state,
                           float *out, void *stream);
 
+/* ---- Full-attention decode step --------------------------------------------------
+ * Replaces, in NMOEFullAttentionStepMetal (src/runtime.m:3040-3095), nmoe_full_qk_prep
+ * (per-head RMS norm with weight + 1, rotate-half RoPE on dims 0..63 with theta 1e7,
+ * sigmoid of the query gate; metal/kernels.metal:1006-1058), the copies of k and v into
+ * the caches, and nmoe_attn_decode_fused (kernels.metal:1119-1194). Qwen3.6 geometry: 16
+ * query heads, 2 KV heads, head dim 256. DEVICE pointers: q f32 [16][512] (query | gate
+ * per head; not modified), k_new / v_new f32 [2][256] (the k / v projections of this
+ * token), k_cache / v_cache f32 [max_positions][2][256] (row `position` is written),
+ * out f32 [16][256] (attention times the gate, the input of o_proj). workspace: DEVICE,
+ * nmoe_full_attn_workspace_bytes(), 16-byte aligned (the slices' partial results; calls
+ * sharing a workspace must not overlap). Two launches: split-K over positions (up to 148
+ * CTAs), then the merge of the slices; allocates nothing; capturable. */
+typedef struct nmoe_full_attn_weights {
+    const uint16_t *q_norm;   /* bf16 [256] self_attn.q_norm.weight */
+    const uint16_t *k_norm;   /* bf16 [256] self_attn.k_norm.weight */
+} nmoe_full_attn_weights;
+int nmoe_full_attn_step(const nmoe_full_attn_weights *w, const float *q, const float *k_new,
+                        const float *v_new, float *k_cache, float *v_cache, int position,
+                        int max_positions, float *out, void *workspace, void *stream);
+size_t nmoe_full_attn_workspace_bytes(void);
+
 #ifdef __cplusplus
 }
 #endif

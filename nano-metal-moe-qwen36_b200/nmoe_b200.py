@@ -33,7 +33,7 @@ ABI_SYMBOLS = (
     "nmoe_moe_static_scratch_bytes", "nmoe_moe_static_status", "nmoe_moe_debug_ep_times",
     "nmoe_lm_head_argmax", "nmoe_lm_head_workspace_bytes", "nmoe_lm_head_error",
     "nmoe_moe_load_layer_checked", "nmoe_moe_load_layer_file_checked", "nmoe_crc32c", "nmoe_crc32c_combine",
-    "nmoe_crc32c_device", "nmoe_linear_attn_step",
+    "nmoe_crc32c_device", "nmoe_linear_attn_step", "nmoe_full_attn_step", "nmoe_full_attn_workspace_bytes",
 )
 
 
@@ -63,6 +63,10 @@ class DenseWeights(C.Structure):
 
 class LinearAttnWeights(C.Structure):
     _fields_ = [("conv_w", C.c_void_p), ("A_log", C.c_void_p), ("dt_bias", C.c_void_p), ("norm_w", C.c_void_p)]
+
+
+class FullAttnWeights(C.Structure):
+    _fields_ = [("q_norm", C.c_void_p), ("k_norm", C.c_void_p)]
 
 
 def build(quiet: bool = True) -> str:
@@ -143,6 +147,9 @@ def lib() -> C.CDLL:
     L.nmoe_crc32c_combine.argtypes = [C.c_uint32, C.c_uint32, sz]
     L.nmoe_linear_attn_step.restype = i
     L.nmoe_linear_attn_step.argtypes = [C.POINTER(LinearAttnWeights), vp, vp, vp, vp, vp, vp, vp, vp]
+    L.nmoe_full_attn_step.restype = i
+    L.nmoe_full_attn_step.argtypes = [C.POINTER(FullAttnWeights), vp, vp, vp, vp, vp, i, i, vp, vp, vp]
+    L.nmoe_full_attn_workspace_bytes.restype = sz
     L.nmoe_lm_head_argmax.restype = i
     L.nmoe_lm_head_argmax.argtypes = [C.POINTER(Tensor), i, i, i, vp, i, vp, C.c_float, i, vp, vp, vp, vp]
     L.nmoe_lm_head_workspace_bytes.restype = sz
@@ -452,3 +459,18 @@ def linear_attn_step(weights: dict, qkv, z, alpha, beta, conv_state, delta_state
                                      _ptr(delta_state), _ptr(out), stream)
     if rc != OK:
         raise NmoeError(rc, "nmoe_linear_attn_step")
+
+
+def full_attn_workspace_bytes() -> int:
+    return int(lib().nmoe_full_attn_workspace_bytes())
+
+
+def full_attn_step(weights: dict, q, k_new, v_new, k_cache, v_cache, position: int, max_positions: int, out,
+                   workspace, stream=0):
+    """nmoe_full_attn_step: full-attention decode step (device tensors); `weights` =
+    {"q_norm", "k_norm"}; row `position` of the caches is written."""
+    w = FullAttnWeights(_ptr(weights["q_norm"]), _ptr(weights["k_norm"]))
+    rc = lib().nmoe_full_attn_step(C.byref(w), _ptr(q), _ptr(k_new), _ptr(v_new), _ptr(k_cache), _ptr(v_cache),
+                                   position, max_positions, _ptr(out), _ptr(workspace), stream)
+    if rc != OK:
+        raise NmoeError(rc, "nmoe_full_attn_step")

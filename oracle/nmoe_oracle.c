@@ -580,3 +580,57 @@ void orc_linear_attn_step(const float *qkv, const float *z, const float *alpha, 
     }
     free(cv);
 }
+
+/* --------------------------------------------------- full attention step ---- */
+
+static void orc_fa_prep(float *vec, const uint16_t *w, int position) {
+    float ss = 0.0f;
+    for (int i = 0; i < 256; i++) ss += vec[i] * vec[i];
+    const float inv = 1.0f / sqrtf(ss / 256.0f + 1e-6f);
+    for (int i = 0; i < 256; i++) vec[i] = vec[i] * inv * (orc_bf16_to_f32(w[i]) + 1.0f);
+    for (int t = 0; t < 32; t++) {   /* kernels.metal:1042-1053, rotary_dim 64 */
+        /* theta^(-2t/64) correctly rounded to float (the kernel's pow in float can differ
+         * by an ulp, and at position p the angle moves by p ulps of freq) */
+        const float freq = (float)pow(10000000.0, -2.0 * (double)t / 64.0);
+        const float ang = (float)position * freq;
+        const float c = cosf(ang), s = sinf(ang);
+        const float v0 = vec[t], v1 = vec[t + 32];
+        vec[t] = v0 * c - v1 * s;
+        vec[t + 32] = v0 * s + v1 * c;
+    }
+}
+
+void orc_full_attn_step(const float *q, const float *k_new, const float *v_new, const uint16_t *q_norm,
+                        const uint16_t *k_norm, float *k_cache, float *v_cache, int position, float *out) {
+    for (int kh = 0; kh < 2; kh++) {
+        float kv[256];
+        memcpy(kv, k_new + kh * 256, sizeof kv);
+        orc_fa_prep(kv, k_norm, position);
+        memcpy(k_cache + ((size_t)position * 2 + kh) * 256, kv, sizeof kv);
+        memcpy(v_cache + ((size_t)position * 2 + kh) * 256, v_new + kh * 256, sizeof kv);
+    }
+    const int seq = position + 1;
+    float *sc = (float *)malloc((size_t)seq * sizeof(float));
+    for (int h = 0; h < 16; h++) {
+        float qh[256];
+        memcpy(qh, q + h * 512, sizeof qh);
+        orc_fa_prep(qh, q_norm, position);
+        const int kh = h / 8;
+        float m = -1e30f;
+        for (int p = 0; p < seq; p++) {
+            const float *kp = k_cache + ((size_t)p * 2 + kh) * 256;
+            float d = 0.0f;
+            for (int i = 0; i < 256; i++) d += qh[i] * kp[i];
+            sc[p] = d * (1.0f / 16.0f);
+            if (sc[p] > m) m = sc[p];
+        }
+        double l = 0.0;
+        for (int p = 0; p < seq; p++) l += exp((double)(sc[p] - m));
+        for (int i = 0; i < 256; i++) {
+            double a = 0.0;
+            for (int p = 0; p < seq; p++) a += exp((double)(sc[p] - m)) * v_cache[((size_t)p * 2 + kh) * 256 + i];
+            out[h * 256 + i] = (float)(a / l) * orc_sigmoid_kernel(q[h * 512 + 256 + i]);
+        }
+    }
+    free(sc);
+}

@@ -156,6 +156,18 @@ void orc_linear_attn_step(const float *qkv, const float *z, const float *alpha, 
                           const uint16_t *conv_w, const float *A_log, const uint16_t *dt_bias,
                           const uint16_t *norm_w, float *conv_state, float *delta_state, float *out);
 
+/* Full-attention decode step (Qwen3.6: 16 query heads, 2 KV heads, head dim 256, partial
+ * rotary 64, RoPE theta 1e7), the reference's sequence (src/runtime.m:3040-3095):
+ *   nmoe_full_qk_prep (metal/kernels.metal:1006-1058): per head RMS norm (eps 1e-6, weight
+ *     + 1), rotate-half RoPE on dims 0..63 at `position`, sigmoid of the q gate half;
+ *   k, v of the position copied into the caches ([pos][2][256] f32);
+ *   nmoe_attn_decode_fused (kernels.metal:1119-1194): softmax(q k / 16) v over positions
+ *     0..position, times the gate.
+ * q f32 [16][512] (query | gate per head), k_new/v_new f32 [2][256]; q_norm/k_norm bf16
+ * [256]; caches updated at `position`; out f32 [16][256]. q is not modified. */
+void orc_full_attn_step(const float *q, const float *k_new, const float *v_new, const uint16_t *q_norm,
+                        const uint16_t *k_norm, float *k_cache, float *v_cache, int position, float *out);
+
 /* Set the OpenMP thread count used by the matvecs (0 = library default). */
 void orc_set_threads(int n);
 int orc_get_threads(void);

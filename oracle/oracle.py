@@ -92,6 +92,7 @@ def lib() -> C.CDLL:
         L.orc_crc32c.argtypes = [C.c_uint32, C.c_void_p, C.c_size_t]
         L.orc_linear_attn_step.argtypes = [_f32p, _f32p, _f32p, _f32p, _u16p, _f32p, _u16p, _u16p, _f32p, _f32p,
                                            _f32p]
+        L.orc_full_attn_step.argtypes = [_f32p, _f32p, _f32p, _u16p, _u16p, _f32p, _f32p, C.c_int, _f32p]
         L.orc_set_threads.argtypes = [C.c_int]
         L.orc_get_threads.restype = C.c_int
         _lib = L
@@ -367,4 +368,12 @@ def linear_attn_step(w, inp, conv_state, delta_state):
     lib().orc_linear_attn_step(inp["qkv"], inp["z"], inp["alpha"], inp["beta"], w["conv_w"].reshape(-1),
                                w["A_log"], w["dt_bias"], w["norm_w"], conv_state.reshape(-1),
                                delta_state.reshape(-1), out)
+    return out
+
+
+def full_attn_step(q, k_new, v_new, q_norm, k_norm, k_cache, v_cache, position):
+    """One full-attention decode step by the reference's sequence; caches updated."""
+    out = np.zeros(16 * 256, np.float32)
+    lib().orc_full_attn_step(np.ascontiguousarray(q, np.float32).reshape(-1), k_new.reshape(-1), v_new.reshape(-1),
+                             q_norm, k_norm, k_cache.reshape(-1), v_cache.reshape(-1), int(position), out)
     return out
