@@ -340,6 +340,48 @@ int nmoe_full_attn_step(const nmoe_full_attn_weights *w, const float *q, const f
                         int max_positions, float *out, void *workspace, void *stream);
 size_t nmoe_full_attn_workspace_bytes(void);
 
+/* ---- Whole decode step ------------------------------------------
+ * The C restatement of NMOEProcessToken (src/runtime.m:3712-3805) on the GPU: embedding
+ * row, 40 layers (layer l is full attention when (l + 1) % 4 == 0, else linear attention:
+ * src/runtime.m:2373), each: input RMSNorm (weight + 1, eps 1e-6), attention (projections
+ * as q4 matrix-vector products in the reference's dequant order, then
+ * nmoe_linear_attn_step or nmoe_full_attn_step), output projection + residual, post
+ * RMSNorm, and the routed-MoE block of the given context (nmoe_moe_forward with the
+ * residual as h_mid); then the final RMSNorm and the LM head's top-1 (nmoe_lm_head_argmax).
+ * Weights given to the set calls are HOST pointers, copied to the device. q4 matrices:
+ * weight u32 [rows][cols/8], scales/biases bf16 [rows][cols/64] (nmoe_tensor). */
+typedef struct nmoe_decoder nmoe_decoder;
+typedef struct nmoe_linear_layer_host {
+    const uint16_t *input_norm, *post_norm;   /* bf16 [2048] */
+    nmoe_tensor qkv, z, beta, alpha;          /* q4 [8192|4096|32|32][2048]  in_proj_qkv / z / b / a */
+    nmoe_tensor out;                          /* q4 [2048][4096]             out_proj               */
+    const uint16_t *conv_w;                   /* bf16 [8192][4]  */
+    const float *A_log;                       /* f32 [32]        */
+    const uint16_t *dt_bias;                  /* bf16 [32]       */
+    const uint16_t *norm_w;                   /* bf16 [128]      */
+} nmoe_linear_layer_host;
+typedef struct nmoe_full_layer_host {
+    const uint16_t *input_norm, *post_norm;   /* bf16 [2048] */
+    nmoe_tensor q, k, v;                      /* q4 [8192|512|512][2048] (q: per head 256 query + 256 gate) */
+    nmoe_tensor o;                            /* q4 [2048][4096] */
+    const uint16_t *q_norm, *k_norm;          /* bf16 [256] */
+} nmoe_full_layer_host;
+/* moe: a context with num_layers >= the decoder's, every layer loaded; k routed experts. */
+nmoe_decoder *nmoe_decoder_create(nmoe_moe_ctx *moe, int num_layers, int k, int max_positions, int *status);
+void nmoe_decoder_destroy(nmoe_decoder *dec);
+const char *nmoe_decoder_error(const nmoe_decoder *dec);
+int nmoe_decoder_set_linear_layer(nmoe_decoder *dec, int layer, const nmoe_linear_layer_host *w);
+int nmoe_decoder_set_full_layer(nmoe_decoder *dec, int layer, const nmoe_full_layer_host *w);
+/* embed / lm_head: NMOE_DTYPE_Q4 or NMOE_DTYPE_BF16, [vocab][2048]; final_norm bf16 [2048]. */
+int nmoe_decoder_set_globals(nmoe_decoder *dec, int vocab, int embed_dtype, const nmoe_tensor *embed,
+                             const uint16_t *final_norm, int head_dtype, const nmoe_tensor *lm_head);
+/* Zero the recurrent and conv states (a new sequence). */
+int nmoe_decoder_reset(nmoe_decoder *dec, void *stream);
+/* One token: d_token (DEVICE u32) at `position` (< max_positions) -> d_next (DEVICE u32).
+ * d_hidden (DEVICE f32 [2048], may be NULL) receives the last layer's output. */
+int nmoe_decoder_step(nmoe_decoder *dec, const uint32_t *d_token, int position, uint32_t *d_next,
+                      float *d_hidden, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -34,6 +34,8 @@ ABI_SYMBOLS = (
     "nmoe_lm_head_argmax", "nmoe_lm_head_workspace_bytes", "nmoe_lm_head_error",
     "nmoe_moe_load_layer_checked", "nmoe_moe_load_layer_file_checked", "nmoe_crc32c", "nmoe_crc32c_combine",
     "nmoe_crc32c_device", "nmoe_linear_attn_step", "nmoe_full_attn_step", "nmoe_full_attn_workspace_bytes",
+    "nmoe_decoder_create", "nmoe_decoder_destroy", "nmoe_decoder_error", "nmoe_decoder_set_linear_layer",
+    "nmoe_decoder_set_full_layer", "nmoe_decoder_set_globals", "nmoe_decoder_reset", "nmoe_decoder_step",
 )
 
 
@@ -67,6 +69,17 @@ class LinearAttnWeights(C.Structure):
 
 class FullAttnWeights(C.Structure):
     _fields_ = [("q_norm", C.c_void_p), ("k_norm", C.c_void_p)]
+
+
+class LinearLayerHost(C.Structure):
+    _fields_ = [("input_norm", C.c_void_p), ("post_norm", C.c_void_p), ("qkv", Tensor), ("z", Tensor),
+                ("beta", Tensor), ("alpha", Tensor), ("out", Tensor), ("conv_w", C.c_void_p), ("A_log", C.c_void_p),
+                ("dt_bias", C.c_void_p), ("norm_w", C.c_void_p)]
+
+
+class FullLayerHost(C.Structure):
+    _fields_ = [("input_norm", C.c_void_p), ("post_norm", C.c_void_p), ("q", Tensor), ("k", Tensor), ("v", Tensor),
+                ("o", Tensor), ("q_norm", C.c_void_p), ("k_norm", C.c_void_p)]
 
 
 def build(quiet: bool = True) -> str:
@@ -150,6 +163,21 @@ def lib() -> C.CDLL:
     L.nmoe_full_attn_step.restype = i
     L.nmoe_full_attn_step.argtypes = [C.POINTER(FullAttnWeights), vp, vp, vp, vp, vp, i, i, vp, vp, vp]
     L.nmoe_full_attn_workspace_bytes.restype = sz
+    L.nmoe_decoder_create.restype = vp
+    L.nmoe_decoder_create.argtypes = [vp, i, i, i, C.POINTER(i)]
+    L.nmoe_decoder_destroy.argtypes = [vp]
+    L.nmoe_decoder_error.restype = C.c_char_p
+    L.nmoe_decoder_error.argtypes = [vp]
+    L.nmoe_decoder_set_linear_layer.restype = i
+    L.nmoe_decoder_set_linear_layer.argtypes = [vp, i, C.POINTER(LinearLayerHost)]
+    L.nmoe_decoder_set_full_layer.restype = i
+    L.nmoe_decoder_set_full_layer.argtypes = [vp, i, C.POINTER(FullLayerHost)]
+    L.nmoe_decoder_set_globals.restype = i
+    L.nmoe_decoder_set_globals.argtypes = [vp, i, i, C.POINTER(Tensor), vp, i, C.POINTER(Tensor)]
+    L.nmoe_decoder_reset.restype = i
+    L.nmoe_decoder_reset.argtypes = [vp, vp]
+    L.nmoe_decoder_step.restype = i
+    L.nmoe_decoder_step.argtypes = [vp, vp, i, vp, vp, vp]
     L.nmoe_lm_head_argmax.restype = i
     L.nmoe_lm_head_argmax.argtypes = [C.POINTER(Tensor), i, i, i, vp, i, vp, C.c_float, i, vp, vp, vp, vp]
     L.nmoe_lm_head_workspace_bytes.restype = sz
@@ -474,3 +502,59 @@ def full_attn_step(weights: dict, q, k_new, v_new, k_cache, v_cache, position: i
                                    position, max_positions, _ptr(out), _ptr(workspace), stream)
     if rc != OK:
         raise NmoeError(rc, "nmoe_full_attn_step")
+
+
+def _q4t(m):
+    return Tensor(_np_ptr(m["weight"]), _np_ptr(m["scales"]), _np_ptr(m["biases"]))
+
+
+class Decoder:
+    """nmoe_decoder: the whole decode step over a loaded Context (one layer per model layer).
+    Layer weights are host numpy arrays (see oracle.make_decoder_weights for the keys)."""
+
+    def __init__(self, moe: Context, num_layers: int, k: int = 8, max_positions: int = 4096):
+        self._L = lib()
+        st = C.c_int(0)
+        h = self._L.nmoe_decoder_create(moe.h, num_layers, k, max_positions, C.byref(st))
+        if not h:
+            raise NmoeError(st.value, "nmoe_decoder_create")
+        self.h, self.moe, self.num_layers = h, moe, num_layers
+
+    def _check(self, rc):
+        if rc != OK:
+            raise NmoeError(rc, self._L.nmoe_decoder_error(self.h).decode())
+
+    def set_layer(self, l: int, w: dict):
+        if w["kind"] == "full":
+            hw = FullLayerHost(_np_ptr(w["input_norm"]), _np_ptr(w["post_norm"]), _q4t(w["q"]), _q4t(w["k"]),
+                               _q4t(w["v"]), _q4t(w["o"]), _np_ptr(w["q_norm"]), _np_ptr(w["k_norm"]))
+            self._check(self._L.nmoe_decoder_set_full_layer(self.h, l, C.byref(hw)))
+        else:
+            hw = LinearLayerHost(_np_ptr(w["input_norm"]), _np_ptr(w["post_norm"]), _q4t(w["qkv"]), _q4t(w["z"]),
+                                 _q4t(w["beta"]), _q4t(w["alpha"]), _q4t(w["out"]), _np_ptr(w["conv_w"]),
+                                 _np_ptr(w["A_log"]), _np_ptr(w["dt_bias"]), _np_ptr(w["norm_w"]))
+            self._check(self._L.nmoe_decoder_set_linear_layer(self.h, l, C.byref(hw)))
+
+    def set_globals(self, g: dict):
+        emb, head = g["embed"], g["lm_head"]
+        et = Tensor(_np_ptr(emb["weight"]), _np_ptr(emb.get("scales")), _np_ptr(emb.get("biases")))
+        ht = Tensor(_np_ptr(head["weight"]), _np_ptr(head.get("scales")), _np_ptr(head.get("biases")))
+        self._check(self._L.nmoe_decoder_set_globals(self.h, g["vocab"], emb["dtype"], C.byref(et),
+                                                     _np_ptr(g["final_norm"]), head["dtype"], C.byref(ht)))
+
+    def reset(self, stream=0):
+        self._check(self._L.nmoe_decoder_reset(self.h, stream))
+
+    def step(self, d_token, position: int, d_next, d_hidden=None, stream=0):
+        self._check(self._L.nmoe_decoder_step(self.h, _ptr(d_token), position, _ptr(d_next), _ptr(d_hidden), stream))
+
+    def close(self):
+        if getattr(self, "h", None):
+            self._L.nmoe_decoder_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -377,3 +377,89 @@ def full_attn_step(q, k_new, v_new, q_norm, k_norm, k_cache, v_cache, position):
     lib().orc_full_attn_step(np.ascontiguousarray(q, np.float32).reshape(-1), k_new.reshape(-1), v_new.reshape(-1),
                              q_norm, k_norm, k_cache.reshape(-1), v_cache.reshape(-1), int(position), out)
     return out
+
+
+# ------------------------------------------------------------ whole decode step ----
+
+def _q4(rng, rows, cols, std=0.02):
+    p, s, b = quantize_rows(randn_bf16(rng, (rows, cols), std), 4)
+    return {"weight": p, "scales": s, "biases": b, "rows": rows, "cols": cols}
+
+
+def make_decoder_weights(seed: int, num_layers: int, vocab: int, head_dtype: int = DTYPE_Q4,
+                         embed_dtype: int = DTYPE_Q4):
+    """Seeded synthetic attention / norm / embedding / head weights of the 40-layer model
+    (all weights ~N(0, 0.02), projections q4 as the reference's converter
+    writes them); layer l is full attention when (l + 1) % 4 == 0."""
+    rng = np.random.default_rng(seed)
+    layers = []
+    for l in range(num_layers):
+        norms = {"input_norm": randn_bf16(rng, (HIDDEN,), 0.02), "post_norm": randn_bf16(rng, (HIDDEN,), 0.02)}
+        if (l + 1) % 4 == 0:
+            layers.append({"kind": "full", **norms, "q": _q4(rng, 8192, 2048), "k": _q4(rng, 512, 2048),
+                           "v": _q4(rng, 512, 2048), "o": _q4(rng, 2048, 4096),
+                           "q_norm": randn_bf16(rng, (256,), 0.02), "k_norm": randn_bf16(rng, (256,), 0.02)})
+        else:
+            la = make_linear_attn(int(rng.integers(1 << 30)))
+            layers.append({"kind": "linear", **norms, "qkv": _q4(rng, 8192, 2048), "z": _q4(rng, 4096, 2048),
+                           "beta": _q4(rng, 32, 2048), "alpha": _q4(rng, 32, 2048), "out": _q4(rng, 2048, 4096),
+                           **la})
+    def table(dtype):
+        w = randn_bf16(rng, (vocab, HIDDEN), 0.02)
+        if dtype == DTYPE_BF16:
+            return {"dtype": DTYPE_BF16, "weight": w}
+        p, s, b = quantize_rows(w, 4)
+        return {"dtype": DTYPE_Q4, "weight": p, "scales": s, "biases": b}
+    g = {"vocab": vocab, "embed": table(embed_dtype), "final_norm": randn_bf16(rng, (HIDDEN,), 0.02),
+         "lm_head": table(head_dtype)}
+    return layers, g
+
+
+def _matvec(m, x):
+    y = np.zeros(m["rows"], np.float32)
+    lib().orc_dequant_matvec(m["weight"].reshape(-1), m["scales"].reshape(-1), m["biases"].reshape(-1),
+                             np.ascontiguousarray(x, np.float32), y, m["rows"], m["cols"], 4, 0)
+    return y
+
+
+class DecoderOracle:
+    """NMOEProcessToken (src/runtime.m:3712-3805) restated with the oracle's pieces:
+    embedding row, per layer input RMSNorm -> attention (linear_attn_step / full_attn_step,
+    projections by the reference's dequant matvec, form 0) -> output projection + residual
+    -> post RMSNorm -> MoE block (block_forward with h_mid), final RMSNorm + LM head."""
+
+    def __init__(self, layers, g, moe_layers, k: int = 8, max_positions: int = 64):
+        self.layers, self.g, self.moe, self.k = layers, g, moe_layers, k
+        self.conv = [np.zeros((3, 8192), np.float32) for _ in layers]
+        self.S = [np.zeros((32, 128, 128), np.float32) for _ in layers]
+        self.kc = [np.zeros((max_positions, 2, 256), np.float32) for _ in layers]
+        self.vc = [np.zeros((max_positions, 2, 256), np.float32) for _ in layers]
+
+    def _embed(self, t):
+        e = self.g["embed"]
+        if e["dtype"] == DTYPE_BF16:
+            return bf16_to_f32(e["weight"][t])
+        q = np.stack([(e["weight"][t] >> (4 * i)) & 0xF for i in range(8)], 1).reshape(-1).astype(np.float32)
+        s = np.repeat(bf16_to_f32(e["scales"][t]), 64)
+        b = np.repeat(bf16_to_f32(e["biases"][t]), 64)
+        return (q * s + b).astype(np.float32)
+
+    def step(self, token: int, position: int):
+        h = self._embed(token)
+        for l, w in enumerate(self.layers):
+            xn = rms_norm(h, w["input_norm"])
+            if w["kind"] == "full":
+                q, kk, vv = _matvec(w["q"], xn), _matvec(w["k"], xn), _matvec(w["v"], xn)
+                a = full_attn_step(q, kk, vv, w["q_norm"], w["k_norm"], self.kc[l], self.vc[l], position)
+                h2 = _matvec(w["o"], a) + h
+            else:
+                inp = {"qkv": _matvec(w["qkv"], xn), "z": _matvec(w["z"], xn), "beta": _matvec(w["beta"], xn),
+                       "alpha": _matvec(w["alpha"], xn)}
+                a = linear_attn_step(w, inp, self.conv[l], self.S[l])
+                h2 = _matvec(w["out"], a) + h
+            xn2 = rms_norm(h2, w["post_norm"])
+            h = block_forward(self.moe[l], self.k, xn2, h_mid=h2)["out"]
+        head = self.g["lm_head"]
+        lh = LmHead(head["dtype"], self.g["vocab"], head["weight"], head.get("scales"), head.get("biases"))
+        tok, logits = lm_head_argmax(lh, h, self.g["final_norm"])
+        return tok, h, logits

@@ -18,7 +18,7 @@ HEADER = os.path.join(REPO, "include", "nmoe", "moe_cuda.h")
 def header_functions():
     text = open(HEADER).read()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"\b(nmoe_(?:moe|lm_head|linear_attn|full_attn)_\w+|nmoe_crc32c\w*)\s*\(", text)))
+    return sorted(set(re.findall(r"\b(nmoe_(?:moe|lm_head|linear_attn|full_attn|decoder)_\w+|nmoe_crc32c\w*)\s*\(", text)))
 
 
 def test_library_exports_every_header_symbol():
