@@ -916,6 +916,88 @@ def run_full_attn(args, dev):
     return res
 
 
+def fast_decoder_weights(seed: int, num_layers: int, vocab: int):
+    """Synthetic q4 attention / embedding / head weights of the 40-layer model, drawn
+    directly in the packed format (uniform nibbles, scale 0.005, bias -0.0375: weights
+    uniform in +-0.0375); norms and linear-attention parameters as the oracle's generator
+    makes them. Generating 40 layers through the quantiser takes minutes of host time."""
+    from oracle import oracle as O
+    rng = np.random.default_rng(seed)
+    s16 = O.f32_to_bf16(np.full(1, 0.005, np.float32))[0]
+    b16 = O.f32_to_bf16(np.full(1, -0.0375, np.float32))[0]
+
+    def q4(rows, cols):
+        return {"weight": rng.integers(0, 1 << 32, (rows, cols // 8), dtype=np.uint32),
+                "scales": np.full((rows, cols // 64), s16, np.uint16),
+                "biases": np.full((rows, cols // 64), b16, np.uint16), "rows": rows, "cols": cols}
+    layers = []
+    for l in range(num_layers):
+        norms = {"input_norm": O.randn_bf16(rng, (HIDDEN,), 0.02), "post_norm": O.randn_bf16(rng, (HIDDEN,), 0.02)}
+        if (l + 1) % 4 == 0:
+            layers.append({"kind": "full", **norms, "q": q4(8192, 2048), "k": q4(512, 2048), "v": q4(512, 2048),
+                           "o": q4(2048, 4096), "q_norm": O.randn_bf16(rng, (256,), 0.02),
+                           "k_norm": O.randn_bf16(rng, (256,), 0.02)})
+        else:
+            layers.append({"kind": "linear", **norms, "qkv": q4(8192, 2048), "z": q4(4096, 2048),
+                           "beta": q4(32, 2048), "alpha": q4(32, 2048), "out": q4(2048, 4096),
+                           **O.make_linear_attn(int(rng.integers(1 << 30)))})
+    emb, head = q4(vocab, HIDDEN), q4(vocab, HIDDEN)
+    g = {"vocab": vocab, "embed": {"dtype": 4, **emb}, "lm_head": {"dtype": 4, **head},
+         "final_norm": O.randn_bf16(rng, (HIDDEN,), 0.02)}
+    return layers, g
+
+
+def run_decode_step(args, dev):
+    """the whole decode step of the 40-layer model (nmoe_decoder_step:
+    embedding, 30 linear-attention and 10 full-attention layers with their q4 projections,
+    the MoE block of every layer, final norm and q4 LM head over 248320 rows), each step's
+    token read on the device from the step before. Tokens per second over K steps at
+    positions W..W+K-1, device time by CUDA events."""
+    import torch
+    import nmoe_b200 as N
+    L = 40
+    moe, _, _ = build_workload(L, 4, 8, N.DTYPE_BF16, N.DTYPE_BF16, pool=args.pool, seed=args.seed)
+    ctx = N.Context(quant_bits=4, num_layers=L, router_dtype=N.DTYPE_BF16, shared_dtype=N.DTYPE_BF16, device=dev)
+    for l, lw in enumerate(moe):
+        ctx.load_layer(l, lw.experts)
+        ctx.set_dense(l, lw.router, lw.shared_gate, lw.shared_up, lw.shared_down, lw.shared_gate_vec)
+    del moe
+    layers, g = fast_decoder_weights(args.seed + 5, L, LM_VOCAB)
+    steps, warm = args.steps, args.warmup
+    dec = N.Decoder(ctx, L, k=8, max_positions=steps + warm + 1)
+    for l in range(L):
+        dec.set_layer(l, layers[l])
+    dec.set_globals(g)
+    del layers, g
+    st = torch.cuda.Stream(device=dev)
+    sp = st.cuda_stream
+    tok = torch.tensor([11], dtype=torch.int32, device=f"cuda:{dev}")
+    with torch.cuda.stream(st):
+        for p in range(warm):
+            dec.step(tok, p, tok, stream=sp)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clk = ClockSampler(dev)
+    clk.start()
+    e0.record(st)
+    with torch.cuda.stream(st):
+        for p in range(warm, warm + steps):
+            dec.step(tok, p, tok, stream=sp)
+    e1.record(st)
+    torch.cuda.synchronize()
+    clocks = clk.stop()
+    ms = e0.elapsed_time(e1) / steps
+    dec.close()
+    ctx.close()
+    return {"metric": "decode_tokens_per_s", "value": 1e3 / ms, "unit": "tokens/s", "ms_per_step": ms,
+            "steps": steps, "warmup": warm, "higher_is_better": True, "dtype": "q4 weights, f32 activations",
+            "data": "synthetic, random-init weights of the 40-layer architecture",
+            "config": {"workload": "config3 decode step, 40 layers, q4 experts k=8, q4 attention projections, "
+                                   "q4 LM head over 248320 rows, batch 1",
+                       "positions": [warm, warm + steps - 1]},
+            "clocks": clocks}
+
+
 def run_ep_batched(args, rank, world, dev):
     """Config 2 beside the decode line, at every N: T tokens per rank (--ep-tokens) through
     --ep-layers resident layers per step, experts sharded 256/N per GPU with token rows
@@ -993,7 +1075,7 @@ def main():
     ap.add_argument("--pool", type=int, default=32, help="distinct expert packs generated on the host")
     ap.add_argument("--seed", type=int, default=2026)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--workload", choices=["decode", "batched", "lm_head", "crc", "linear_attn", "full_attn"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "batched", "lm_head", "crc", "linear_attn", "full_attn", "decode_step"], default="decode")
     ap.add_argument("--lm-dtypes", default="q4,bf16", help="LM head weight types timed (q4, bf16)")
     ap.add_argument("--bits", type=int, choices=[2, 4], default=4, help="decode: expert packs (4: config 0, 2: config 1)")
     ap.add_argument("--k", type=int, default=8, help="decode: routed experts per token (config 1 sweeps 1..8)")
@@ -1026,7 +1108,11 @@ def main():
         import torch.distributed as dist
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local_rank}"))
-    if args.workload == "full_attn":
+    if args.workload == "decode_step":
+        import torch
+        torch.cuda.set_device(local_rank)
+        res = {"workload": "decode_step", **run_decode_step(args, local_rank)} if rank == 0 else None
+    elif args.workload == "full_attn":
         import torch
         torch.cuda.set_device(local_rank)
         res = {"workload": "full_attn", **run_full_attn(args, local_rank)} if rank == 0 else None
