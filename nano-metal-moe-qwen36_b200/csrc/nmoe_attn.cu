@@ -36,8 +36,16 @@ struct FaArgs {
     float *k_cache, *v_cache, *out;
     float *part;          // [kKV][kMaxSplit][kGroup][kPart]
     int position, splits;
+    const int *d_position;   // when set: the position is read on the device (graph replays) and
+                             // the grid holds kMaxSplit slices per KV head, the unused ones exit
     float freq[32];       // RoPE frequencies theta^(-2t/64), correctly rounded to float
 };
+
+// ~64 positions (64 KB of K and V) per slice, 1 to kMaxSplit slices
+__host__ __device__ __forceinline__ int slices_for(int position) {
+    const int s = (position + 64) / 64;
+    return s < 1 ? 1 : (s > kMaxSplit ? kMaxSplit : s);
+}
 
 __device__ __forceinline__ float bf16f(uint16_t v) { return __uint_as_float((uint32_t)v << 16); }
 
@@ -71,11 +79,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_full_attn_step(const FaArgs a) 
     float *tl = tm + kWarps * kGroup;            // [8 warps][8 heads]
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int kvh = blockIdx.x / a.splits, split = blockIdx.x % a.splits;
-    const int seq = a.position + 1;
-    const int P = (seq + a.splits - 1) / a.splits;
+    const int position = a.d_position ? *a.d_position : a.position;
+    const int splits = a.d_position ? slices_for(position) : a.splits;
+    const int grid_splits = a.d_position ? kMaxSplit : a.splits;
+    const int kvh = blockIdx.x / grid_splits, split = blockIdx.x % grid_splits;
+    if (split >= splits) return;   // uniform over the CTA, before any barrier
+    const int seq = position + 1;
+    const int P = (seq + splits - 1) / splits;
     const int p0 = min(seq, split * P), p1 = min(seq, p0 + P);
-    const bool holds_new = p0 <= a.position && a.position < p1;
+    const bool holds_new = p0 <= position && position < p1;
 
     // ---- queries of the 8 heads (warp w: head 8 kvh + w)
     {
@@ -83,7 +95,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_full_attn_step(const FaArgs a) 
         float v[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) v[j] = a.q[h * 2 * kDim + lane + 32 * j];
-        prep_vec(v, a.q_norm, a.position, lane, a.freq);
+        prep_vec(v, a.q_norm, position, lane, a.freq);
 #pragma unroll
         for (int j = 0; j < 8; ++j) qs[warp * kDim + lane + 32 * j] = v[j];
     }
@@ -92,8 +104,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_full_attn_step(const FaArgs a) 
         float v[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) v[j] = a.k_new[kvh * kDim + lane + 32 * j];
-        prep_vec(v, a.k_norm, a.position, lane, a.freq);
-        const size_t row = ((size_t)a.position * kKV + kvh) * kDim;
+        prep_vec(v, a.k_norm, position, lane, a.freq);
+        const size_t row = ((size_t)position * kKV + kvh) * kDim;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             a.k_cache[row + lane + 32 * j] = v[j];
@@ -204,19 +216,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_full_attn_step(const FaArgs a) 
 __global__ void __launch_bounds__(kThreads) k_full_attn_merge(const FaArgs a) {
     __shared__ float sm_m[kMaxSplit], sm_l[kMaxSplit];
     const int tid = threadIdx.x;
+    const int splits = a.d_position ? slices_for(*a.d_position) : a.splits;
     const int kvh = blockIdx.x / kGroup, h = blockIdx.x % kGroup;
     const float *pb = a.part + (size_t)kvh * kMaxSplit * kGroup * kPart + (size_t)h * kPart;
     const size_t sstride = (size_t)kGroup * kPart;
-    if (tid < a.splits) {
+    if (tid < splits) {
         sm_m[tid] = pb[tid * sstride + kDim];
         sm_l[tid] = pb[tid * sstride + kDim + 1];
     }
     __syncthreads();
     float M = -1e30f;
-    for (int sI = 0; sI < a.splits; ++sI) M = fmaxf(M, sm_m[sI]);
+    for (int sI = 0; sI < splits; ++sI) M = fmaxf(M, sm_m[sI]);
     float L = 0.f, A = 0.f;
 #pragma unroll 8
-    for (int sI = 0; sI < a.splits; ++sI) {
+    for (int sI = 0; sI < splits; ++sI) {
         const float e = __expf(sm_m[sI] - M);
         L = fmaf(sm_l[sI], e, L);
         A = fmaf(pb[sI * sstride + tid], e, A);
@@ -234,14 +247,11 @@ extern "C" size_t nmoe_full_attn_workspace_bytes(void) {
     return (size_t)kKV * kMaxSplit * kGroup * kPart * 4 + 256;
 }
 
-extern "C" int nmoe_full_attn_step(const nmoe_full_attn_weights *w, const float *q, const float *k_new,
-                                   const float *v_new, float *k_cache, float *v_cache, int position,
-                                   int max_positions, float *out, void *workspace, void *stream) {
-    if (w == nullptr || w->q_norm == nullptr || w->k_norm == nullptr || q == nullptr || k_new == nullptr ||
-        v_new == nullptr || k_cache == nullptr || v_cache == nullptr || out == nullptr || workspace == nullptr)
-        return NMOE_EINVAL;
-    if (position < 0 || position >= max_positions) return NMOE_EINVAL;
-    if ((reinterpret_cast<uintptr_t>(workspace) & 15u) != 0) return NMOE_EINVAL;
+namespace {
+
+int launch_full_attn(const nmoe_full_attn_weights *w, const float *q, const float *k_new, const float *v_new,
+                     float *k_cache, float *v_cache, int position, const int *d_position, float *out,
+                     void *workspace, cudaStream_t st) {
     static bool attr_set = false;   // per process; the attribute is a function property
     if (!attr_set) {
         if (cudaFuncSetAttribute(k_full_attn_step, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem) !=
@@ -249,9 +259,6 @@ extern "C" int nmoe_full_attn_step(const nmoe_full_attn_weights *w, const float 
             return NMOE_ECUDA;
         attr_set = true;
     }
-    const int seq = position + 1;
-    int splits = (seq + 63) / 64;   // ~64 positions (64 KB of K and V) per CTA, up to 148 CTAs
-    splits = splits < 1 ? 1 : (splits > kMaxSplit ? kMaxSplit : splits);
     FaArgs a;
     a.q = q;
     a.k_new = k_new;
@@ -263,9 +270,36 @@ extern "C" int nmoe_full_attn_step(const nmoe_full_attn_weights *w, const float 
     a.out = out;
     a.part = static_cast<float *>(workspace);
     a.position = position;
-    a.splits = splits;
+    a.splits = slices_for(position);
+    a.d_position = d_position;
     for (int t = 0; t < 32; ++t) a.freq[t] = (float)pow((double)kTheta, -2.0 * t / 64.0);
-    k_full_attn_step<<<kKV * splits, kThreads, kSmem, static_cast<cudaStream_t>(stream)>>>(a);
-    k_full_attn_merge<<<kKV * kGroup, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
+    const int grid = kKV * (d_position ? kMaxSplit : a.splits);
+    k_full_attn_step<<<grid, kThreads, kSmem, st>>>(a);
+    k_full_attn_merge<<<kKV * kGroup, kThreads, 0, st>>>(a);
     return cudaGetLastError() == cudaSuccess ? NMOE_OK : NMOE_ECUDA;
 }
+
+}  // namespace
+
+extern "C" int nmoe_full_attn_step(const nmoe_full_attn_weights *w, const float *q, const float *k_new,
+                                   const float *v_new, float *k_cache, float *v_cache, int position,
+                                   int max_positions, float *out, void *workspace, void *stream) {
+    if (w == nullptr || w->q_norm == nullptr || w->k_norm == nullptr || q == nullptr || k_new == nullptr ||
+        v_new == nullptr || k_cache == nullptr || v_cache == nullptr || out == nullptr || workspace == nullptr)
+        return NMOE_EINVAL;
+    if (position < 0 || position >= max_positions) return NMOE_EINVAL;
+    if ((reinterpret_cast<uintptr_t>(workspace) & 15u) != 0) return NMOE_EINVAL;
+    return launch_full_attn(w, q, k_new, v_new, k_cache, v_cache, position, nullptr, out, workspace,
+                            static_cast<cudaStream_t>(stream));
+}
+
+namespace nmoe {
+// The same step with the position read on the device from *d_position (checked by the
+// caller to lie in [0, max_positions)): one launch shape for every position, so that a
+// captured graph of decode steps replays at any position.
+int full_attn_step_dev(const nmoe_full_attn_weights *w, const float *q, const float *k_new, const float *v_new,
+                       float *k_cache, float *v_cache, const int *d_position, float *out, void *workspace,
+                       cudaStream_t st) {
+    return launch_full_attn(w, q, k_new, v_new, k_cache, v_cache, 0, d_position, out, workspace, st);
+}
+}  // namespace nmoe

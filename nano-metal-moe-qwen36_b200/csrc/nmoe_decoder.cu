@@ -14,11 +14,18 @@
 #include <cuda_runtime.h>
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <vector>
 
 #include "nmoe/moe_cuda.h"
+
+namespace nmoe {
+int full_attn_step_dev(const nmoe_full_attn_weights *w, const float *q, const float *k_new, const float *v_new,
+                       float *k_cache, float *v_cache, const int *d_position, float *out, void *workspace,
+                       cudaStream_t st);
+}
 
 namespace {
 
@@ -31,12 +38,16 @@ __device__ __forceinline__ float nib(uint32_t w, int i) {
     return __int_as_float(0x4B000000 | ((w >> (4 * i)) & 0xFu)) - 8388608.0f;
 }
 
-// y[r] = sum_c fma(q, s, b) * x[c] (+ resid[r]), r < rows, K columns (a multiple of 256).
+// y[r] = sum_c fma(q, s, b) * x[c] (+ resid[r]), r < rows, K columns (a multiple of 1024).
+// x sits in shared memory in 32-column pieces padded to 36 floats: lane l reads the piece
+// of its chunk l + 32 c as eight float4, and the 8 lanes of each quarter-warp phase hit 8
+// different 16-byte bank groups (piece stride 9 units), where an unpadded layout (stride
+// 8 units) puts them all on one.
 template <int K>
 __global__ void __launch_bounds__(kMvWarps * 32) k_q4_matvec(const uint32_t *w, const uint16_t *s, const uint16_t *b,
                                                             int rows, const float *x, const float *resid, float *y) {
-    __shared__ __align__(16) float xs[K];
-    for (int i = threadIdx.x; i < K; i += kMvWarps * 32) xs[i] = x[i];
+    __shared__ __align__(16) float xs[K / 32 * 36];
+    for (int i = threadIdx.x; i < K; i += kMvWarps * 32) xs[(i >> 5) * 36 + (i & 31)] = x[i];
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr int kChunks = K / 32 / 32;   // 16-byte chunks (32 columns) per lane
@@ -52,11 +63,17 @@ __global__ void __launch_bounds__(kMvWarps * 32) k_q4_matvec(const uint32_t *w, 
             const int chunk = lane + 32 * c, g = chunk >> 1;   // 32 columns, half a group
             const float sv = bf16f(sr[g]), bv = bf16f(br[g]);
             const uint32_t ws[4] = {u[c].x, u[c].y, u[c].z, u[c].w};
-            const float *xp = xs + 32 * chunk;
+            const float4 *xp = reinterpret_cast<const float4 *>(xs + 36 * chunk);
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-#pragma unroll
-                for (int i = 0; i < 8; ++i) acc = fmaf(fmaf(nib(ws[j], i), sv, bv), xp[8 * j + i], acc);
+            for (int m = 0; m < 8; ++m) {
+                const float4 xv = xp[m];
+                const uint32_t wd = ws[m >> 1];
+                const int i0 = 4 * (m & 1);
+                acc = fmaf(fmaf(nib(wd, i0), sv, bv), xv.x, acc);
+                acc = fmaf(fmaf(nib(wd, i0 + 1), sv, bv), xv.y, acc);
+                acc = fmaf(fmaf(nib(wd, i0 + 2), sv, bv), xv.z, acc);
+                acc = fmaf(fmaf(nib(wd, i0 + 3), sv, bv), xv.w, acc);
+            }
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
@@ -135,6 +152,8 @@ struct FullLayer {
 
 bool is_full(int l) { return ((l + 1) % 4) == 0; }
 
+__global__ void k_set_position(int *p, int v) { *p = v; }
+
 }  // namespace
 
 struct nmoe_decoder {
@@ -153,11 +172,22 @@ struct nmoe_decoder {
     float *h0 = nullptr, *h1 = nullptr, *xn = nullptr, *h2 = nullptr, *qkv = nullptr, *z = nullptr, *beta = nullptr,
           *alpha = nullptr, *attn = nullptr, *q = nullptr, *kk = nullptr, *vv = nullptr;
     void *fa_ws = nullptr, *lm_ws = nullptr;
+    int *d_pos = nullptr;   // the step's position, written by a one-thread launch before the step
+    // the step as one CUDA graph, captured for one (token, next, hidden) pointer triple
+    cudaGraphExec_t graph = nullptr;
+    cudaStream_t cap = nullptr;
+    const void *g_token = nullptr, *g_next = nullptr, *g_hidden = nullptr;
+    bool use_graph = true;
     std::vector<void *> allocs;
     char err[512] = {0};
 };
 
 namespace {
+
+void drop_graph(nmoe_decoder *d) {
+    if (d->graph) cudaGraphExecDestroy(d->graph);
+    d->graph = nullptr;
+}
 
 int dfail(nmoe_decoder *d, int code, const char *fmt, ...) {
     va_list ap;
@@ -220,7 +250,11 @@ extern "C" nmoe_decoder *nmoe_decoder_create(nmoe_moe_ctx *moe, int num_layers, 
               dalloc(d, &d->h2, kHidden * 4) && dalloc(d, &d->qkv, 8192 * 4) && dalloc(d, &d->z, 4096 * 4) &&
               dalloc(d, &d->beta, 32 * 4) && dalloc(d, &d->alpha, 32 * 4) && dalloc(d, &d->attn, 4096 * 4) &&
               dalloc(d, &d->q, 8192 * 4) && dalloc(d, &d->kk, 512 * 4) && dalloc(d, &d->vv, 512 * 4) &&
-              dalloc(d, &d->fa_ws, nmoe_full_attn_workspace_bytes()) && dalloc(d, &d->lm_ws, nmoe_lm_head_workspace_bytes());
+              dalloc(d, &d->fa_ws, nmoe_full_attn_workspace_bytes()) && dalloc(d, &d->lm_ws, nmoe_lm_head_workspace_bytes()) &&
+              dalloc(d, &d->d_pos, 16);
+    if (ok) ok = cudaStreamCreateWithFlags(&d->cap, cudaStreamNonBlocking) == cudaSuccess;
+    const char *ge = getenv("NMOE_DECODER_GRAPH");
+    d->use_graph = !(ge && ge[0] == '0');
     for (int l = 0; ok && l < num_layers; ++l) {
         if (is_full(l)) {
             const size_t cache = (size_t)max_positions * 2 * 256 * 4;
@@ -241,6 +275,8 @@ extern "C" nmoe_decoder *nmoe_decoder_create(nmoe_moe_ctx *moe, int num_layers, 
 
 extern "C" void nmoe_decoder_destroy(nmoe_decoder *d) {
     if (d == nullptr) return;
+    if (d->graph) cudaGraphExecDestroy(d->graph);
+    if (d->cap) cudaStreamDestroy(d->cap);
     for (void *p : d->allocs) cudaFree(p);
     delete d;
 }
@@ -259,6 +295,7 @@ extern "C" int nmoe_decoder_reset(nmoe_decoder *d, void *stream) {
 
 extern "C" int nmoe_decoder_set_linear_layer(nmoe_decoder *d, int l, const nmoe_linear_layer_host *w) {
     if (d == nullptr || w == nullptr || l < 0 || l >= d->num_layers) return NMOE_EINVAL;
+    drop_graph(d);
     if (is_full(l)) return dfail(d, NMOE_EINVAL, "layer %d is a full-attention layer", l);
     LinearLayer &L = d->lin[l];
     const bool ok = dcopy(d, &L.in_norm, w->input_norm, kHidden * 2) && dcopy(d, &L.post_norm, w->post_norm, kHidden * 2) &&
@@ -274,6 +311,7 @@ extern "C" int nmoe_decoder_set_linear_layer(nmoe_decoder *d, int l, const nmoe_
 
 extern "C" int nmoe_decoder_set_full_layer(nmoe_decoder *d, int l, const nmoe_full_layer_host *w) {
     if (d == nullptr || w == nullptr || l < 0 || l >= d->num_layers) return NMOE_EINVAL;
+    drop_graph(d);
     if (!is_full(l)) return dfail(d, NMOE_EINVAL, "layer %d is a linear-attention layer", l);
     FullLayer &F = d->full[l];
     const bool ok = dcopy(d, &F.in_norm, w->input_norm, kHidden * 2) && dcopy(d, &F.post_norm, w->post_norm, kHidden * 2) &&
@@ -288,6 +326,7 @@ extern "C" int nmoe_decoder_set_full_layer(nmoe_decoder *d, int l, const nmoe_fu
 extern "C" int nmoe_decoder_set_globals(nmoe_decoder *d, int vocab, int embed_dtype, const nmoe_tensor *embed,
                                         const uint16_t *final_norm, int head_dtype, const nmoe_tensor *lm_head) {
     if (d == nullptr || embed == nullptr || lm_head == nullptr || vocab < 1) return NMOE_EINVAL;
+    drop_graph(d);
     if ((embed_dtype != NMOE_DTYPE_Q4 && embed_dtype != NMOE_DTYPE_BF16) ||
         (head_dtype != NMOE_DTYPE_Q4 && head_dtype != NMOE_DTYPE_BF16))
         return dfail(d, NMOE_EINVAL, "embedding and head dtypes: NMOE_DTYPE_Q4 or NMOE_DTYPE_BF16");
@@ -312,14 +351,10 @@ extern "C" int nmoe_decoder_set_globals(nmoe_decoder *d, int vocab, int embed_dt
     return NMOE_OK;
 }
 
-extern "C" int nmoe_decoder_step(nmoe_decoder *d, const uint32_t *d_token, int position, uint32_t *d_next,
-                                 float *d_hidden, void *stream) {
-    if (d == nullptr || d_token == nullptr || d_next == nullptr) return NMOE_EINVAL;
-    if (position < 0 || position >= d->max_pos) return dfail(d, NMOE_EINVAL, "position %d outside [0, %d)", position, d->max_pos);
-    if (!d->globals) return dfail(d, NMOE_EINVAL, "globals not set");
-    for (int l = 0; l < d->num_layers; ++l)
-        if (!(is_full(l) ? d->full[l].set : d->lin[l].set)) return dfail(d, NMOE_EINVAL, "layer %d not set", l);
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
+namespace {
+
+// Every launch of one step on st; the position is read on the device from d->d_pos.
+int enqueue_step(nmoe_decoder *d, const uint32_t *d_token, uint32_t *d_next, float *d_hidden, cudaStream_t st) {
     k_embed<<<1, 256, 0, st>>>(d_token, d->vocab, d->embed_q4, d->embed_w, d->embed_s, d->embed_b, d->h0);
     float *h = d->h0, *hn = d->h1;
     for (int l = 0; l < d->num_layers; ++l) {
@@ -330,8 +365,8 @@ extern "C" int nmoe_decoder_step(nmoe_decoder *d, const uint32_t *d_token, int p
                 matvec(F.v, d->xn, nullptr, d->vv, st) != cudaSuccess)
                 return dfail(d, NMOE_ECUDA, "layer %d projections", l);
             nmoe_full_attn_weights aw{F.q_norm, F.k_norm};
-            int rc = nmoe_full_attn_step(&aw, d->q, d->kk, d->vv, F.k_cache, F.v_cache, position, d->max_pos, d->attn,
-                                         d->fa_ws, stream);
+            int rc = nmoe::full_attn_step_dev(&aw, d->q, d->kk, d->vv, F.k_cache, F.v_cache, d->d_pos, d->attn,
+                                              d->fa_ws, st);
             if (rc != NMOE_OK) return dfail(d, rc, "layer %d attention", l);
             if (matvec(F.o, d->attn, h, d->h2, st) != cudaSuccess) return dfail(d, NMOE_ECUDA, "layer %d o_proj", l);
             k_rmsnorm<<<1, 256, 0, st>>>(d->h2, F.post_norm, d->xn);
@@ -344,12 +379,12 @@ extern "C" int nmoe_decoder_step(nmoe_decoder *d, const uint32_t *d_token, int p
                 return dfail(d, NMOE_ECUDA, "layer %d projections", l);
             nmoe_linear_attn_weights lw{L.conv_w, L.A_log, L.dt_bias, L.norm_w};
             int rc = nmoe_linear_attn_step(&lw, d->qkv, d->z, d->alpha, d->beta, L.conv_state, L.delta_state, d->attn,
-                                           stream);
+                                           st);
             if (rc != NMOE_OK) return dfail(d, rc, "layer %d linear attention", l);
             if (matvec(L.out, d->attn, h, d->h2, st) != cudaSuccess) return dfail(d, NMOE_ECUDA, "layer %d out_proj", l);
             k_rmsnorm<<<1, 256, 0, st>>>(d->h2, L.post_norm, d->xn);
         }
-        int rc = nmoe_moe_forward(d->moe, l, d->k, d->xn, NMOE_DTYPE_F32, d->h2, hn, nullptr, nullptr, stream);
+        int rc = nmoe_moe_forward(d->moe, l, d->k, d->xn, NMOE_DTYPE_F32, d->h2, hn, nullptr, nullptr, st);
         if (rc != NMOE_OK) return dfail(d, rc, "layer %d moe: %s", l, nmoe_moe_last_error(d->moe));
         float *t = h;
         h = hn;
@@ -359,7 +394,49 @@ extern "C" int nmoe_decoder_step(nmoe_decoder *d, const uint32_t *d_token, int p
         return dfail(d, NMOE_ECUDA, "hidden copy");
     nmoe_tensor head{d->head_w, d->head_s, d->head_b};
     int rc = nmoe_lm_head_argmax(&head, d->head_dtype, d->vocab, kHidden, h, NMOE_DTYPE_F32, d->final_norm, 1e-6f, 1,
-                                 nullptr, d_next, d->lm_ws, stream);
+                                 nullptr, d_next, d->lm_ws, st);
     if (rc != NMOE_OK) return dfail(d, rc, "lm head: %s", nmoe_lm_head_error());
     return cudaGetLastError() == cudaSuccess ? NMOE_OK : dfail(d, NMOE_ECUDA, "decode step launch");
+}
+
+}  // namespace
+
+extern "C" int nmoe_decoder_step(nmoe_decoder *d, const uint32_t *d_token, int position, uint32_t *d_next,
+                                 float *d_hidden, void *stream) {
+    if (d == nullptr || d_token == nullptr || d_next == nullptr) return NMOE_EINVAL;
+    if (position < 0 || position >= d->max_pos) return dfail(d, NMOE_EINVAL, "position %d outside [0, %d)", position, d->max_pos);
+    if (!d->globals) return dfail(d, NMOE_EINVAL, "globals not set");
+    for (int l = 0; l < d->num_layers; ++l)
+        if (!(is_full(l) ? d->full[l].set : d->lin[l].set)) return dfail(d, NMOE_EINVAL, "layer %d not set", l);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    k_set_position<<<1, 1, 0, st>>>(d->d_pos, position);
+    if (d->graph && d->g_token == d_token && d->g_next == d_next && d->g_hidden == d_hidden) {
+        if (cudaGraphLaunch(d->graph, st) != cudaSuccess) return dfail(d, NMOE_ECUDA, "decode step graph launch");
+        return NMOE_OK;
+    }
+    // first step with these buffers: run it directly, then capture the same launches
+    // (nothing runs during a capture) for the steps after it
+    drop_graph(d);
+    int rc = enqueue_step(d, d_token, d_next, d_hidden, st);
+    if (rc != NMOE_OK || !d->use_graph) return rc;
+    cudaGraph_t g = nullptr;
+    if (cudaStreamBeginCapture(d->cap, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
+        return dfail(d, NMOE_ECUDA, "decode step capture");
+    rc = enqueue_step(d, d_token, d_next, d_hidden, d->cap);
+    const cudaError_t ce = cudaStreamEndCapture(d->cap, &g);
+    if (rc != NMOE_OK || ce != cudaSuccess) {
+        if (g) cudaGraphDestroy(g);
+        cudaGetLastError();
+        return rc != NMOE_OK ? rc : dfail(d, NMOE_ECUDA, "decode step capture: %s", cudaGetErrorString(ce));
+    }
+    const cudaError_t ie = cudaGraphInstantiate(&d->graph, g, 0);
+    cudaGraphDestroy(g);
+    if (ie != cudaSuccess) {
+        d->graph = nullptr;
+        return dfail(d, NMOE_ECUDA, "decode step graph: %s", cudaGetErrorString(ie));
+    }
+    d->g_token = d_token;
+    d->g_next = d_next;
+    d->g_hidden = d_hidden;
+    return NMOE_OK;
 }
