@@ -38,49 +38,6 @@ __device__ __forceinline__ float nib(uint32_t w, int i) {
     return __int_as_float(0x4B000000 | ((w >> (4 * i)) & 0xFu)) - 8388608.0f;
 }
 
-// y[r] = sum_c fma(q, s, b) * x[c] (+ resid[r]), r < rows, K columns (a multiple of 1024).
-// x sits in shared memory in 32-column pieces padded to 36 floats: lane l reads the piece
-// of its chunk l + 32 c as eight float4, and the 8 lanes of each quarter-warp phase hit 8
-// different 16-byte bank groups (piece stride 9 units), where an unpadded layout (stride
-// 8 units) puts them all on one.
-template <int K>
-__global__ void __launch_bounds__(kMvWarps * 32) k_q4_matvec(const uint32_t *w, const uint16_t *s, const uint16_t *b,
-                                                            int rows, const float *x, const float *resid, float *y) {
-    __shared__ __align__(16) float xs[K / 32 * 36];
-    for (int i = threadIdx.x; i < K; i += kMvWarps * 32) xs[(i >> 5) * 36 + (i & 31)] = x[i];
-    __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    constexpr int kChunks = K / 32 / 32;   // 16-byte chunks (32 columns) per lane
-    for (int r = blockIdx.x * kMvWarps + warp; r < rows; r += gridDim.x * kMvWarps) {
-        const uint4 *wr = reinterpret_cast<const uint4 *>(w + (size_t)r * (K / 8));
-        const uint16_t *sr = s + (size_t)r * (K / 64), *br = b + (size_t)r * (K / 64);
-        uint4 u[kChunks];
-#pragma unroll
-        for (int c = 0; c < kChunks; ++c) u[c] = __ldcs(wr + lane + 32 * c);
-        float acc = 0.f;
-#pragma unroll
-        for (int c = 0; c < kChunks; ++c) {
-            const int chunk = lane + 32 * c, g = chunk >> 1;   // 32 columns, half a group
-            const float sv = bf16f(sr[g]), bv = bf16f(br[g]);
-            const uint32_t ws[4] = {u[c].x, u[c].y, u[c].z, u[c].w};
-            const float4 *xp = reinterpret_cast<const float4 *>(xs + 36 * chunk);
-#pragma unroll
-            for (int m = 0; m < 8; ++m) {
-                const float4 xv = xp[m];
-                const uint32_t wd = ws[m >> 1];
-                const int i0 = 4 * (m & 1);
-                acc = fmaf(fmaf(nib(wd, i0), sv, bv), xv.x, acc);
-                acc = fmaf(fmaf(nib(wd, i0 + 1), sv, bv), xv.y, acc);
-                acc = fmaf(fmaf(nib(wd, i0 + 2), sv, bv), xv.z, acc);
-                acc = fmaf(fmaf(nib(wd, i0 + 3), sv, bv), xv.w, acc);
-            }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        if (lane == 0) y[r] = acc + (resid ? resid[r] : 0.f);
-    }
-}
-
 // out = x * rsqrt(mean(x^2) + 1e-6) * (w + 1) over 2048 (the reference's input / post
 // norms: NMOEEncodeRMSNormTensor(..., YES, 1e-6f), metal/kernels.metal:862-900).
 __global__ void __launch_bounds__(256) k_rmsnorm(const float *x, const uint16_t *w, float *out) {
@@ -102,6 +59,93 @@ __global__ void __launch_bounds__(256) k_rmsnorm(const float *x, const uint16_t 
     const float inv = rsqrtf(t / (float)kHidden + 1e-6f);
 #pragma unroll
     for (int j = 0; j < 8; ++j) out[tid + 256 * j] = v[j] * inv * (bf16f(w[tid + 256 * j]) + 1.0f);
+}
+
+// Up to four q4 matrices over one x, one launch: y_m[r] = sum_c fma(q, s, b) * x[c]
+// (+ resid[r] for a single matrix), K columns (2048 or 4096). With norm_w set, x is first
+// replaced by its RMSNorm (weight + 1, eps 1e-6) computed in every CTA exactly as
+// k_rmsnorm does (same thread split and summation order: the same floats), so the input
+// norm of a layer costs no launch of its own. x sits in shared memory in 32-column pieces
+// padded to 36 floats: lane l reads the piece of its chunk l + 32 c as eight float4, and
+// the 8 lanes of each quarter-warp phase hit 8 different 16-byte bank groups (piece stride
+// 9 units), where an unpadded layout (stride 8 units) puts them all on one.
+struct MvSeg {
+    const uint32_t *w;
+    const uint16_t *s, *b;
+    float *y;
+    int row_end;   // cumulative rows through this matrix
+};
+struct MvArgs {
+    MvSeg seg[4];
+    int nseg;
+    const float *x, *resid;
+    const uint16_t *norm_w;
+};
+
+template <int K>
+__global__ void __launch_bounds__(kMvWarps * 32) k_q4_matvec(const MvArgs a) {
+    __shared__ __align__(16) float xs[K / 32 * 36];
+    __shared__ float red[kMvWarps];
+    const int tid = threadIdx.x;
+    if (a.norm_w != nullptr) {   // K == kHidden, 256 threads: k_rmsnorm's arithmetic
+        float v[8], ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            v[j] = a.x[tid + 256 * j];
+            ss += v[j] * v[j];
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if ((tid & 31) == 0) red[tid >> 5] = ss;
+        __syncthreads();
+        float t = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) t += red[i];
+        const float inv = rsqrtf(t / (float)kHidden + 1e-6f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int i = tid + 256 * j;
+            xs[(i >> 5) * 36 + (i & 31)] = v[j] * inv * (bf16f(a.norm_w[i]) + 1.0f);
+        }
+    } else {
+        for (int i = tid; i < K; i += kMvWarps * 32) xs[(i >> 5) * 36 + (i & 31)] = a.x[i];
+    }
+    __syncthreads();
+    const int warp = tid >> 5, lane = tid & 31;
+    constexpr int kChunks = K / 32 / 32;   // 16-byte chunks (32 columns) per lane
+    const int rows = a.seg[a.nseg - 1].row_end;
+    for (int gr = blockIdx.x * kMvWarps + warp; gr < rows; gr += gridDim.x * kMvWarps) {
+        int m = 0;
+        while (m + 1 < a.nseg && gr >= a.seg[m].row_end) ++m;
+        const MvSeg &sg = a.seg[m];
+        const int r = m ? gr - a.seg[m - 1].row_end : gr;
+        const uint4 *wr = reinterpret_cast<const uint4 *>(sg.w + (size_t)r * (K / 8));
+        const uint16_t *sr = sg.s + (size_t)r * (K / 64), *br = sg.b + (size_t)r * (K / 64);
+        uint4 u[kChunks];
+#pragma unroll
+        for (int c = 0; c < kChunks; ++c) u[c] = __ldcs(wr + lane + 32 * c);
+        float acc = 0.f;
+#pragma unroll
+        for (int c = 0; c < kChunks; ++c) {
+            const int chunk = lane + 32 * c, g = chunk >> 1;   // 32 columns, half a group
+            const float sv = bf16f(sr[g]), bv = bf16f(br[g]);
+            const uint32_t ws[4] = {u[c].x, u[c].y, u[c].z, u[c].w};
+            const float4 *xp = reinterpret_cast<const float4 *>(xs + 36 * chunk);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const float4 xv = xp[q];
+                const uint32_t wd = ws[q >> 1];
+                const int i0 = 4 * (q & 1);
+                acc = fmaf(fmaf(nib(wd, i0), sv, bv), xv.x, acc);
+                acc = fmaf(fmaf(nib(wd, i0 + 1), sv, bv), xv.y, acc);
+                acc = fmaf(fmaf(nib(wd, i0 + 2), sv, bv), xv.z, acc);
+                acc = fmaf(fmaf(nib(wd, i0 + 3), sv, bv), xv.w, acc);
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) sg.y[r] = acc + (a.resid ? a.resid[r] : 0.f);
+    }
 }
 
 // Embedding row of *token (q4: dequant_row, metal/kernels.metal nmoe_dequant_row; bf16:
@@ -220,11 +264,30 @@ bool q4copy(nmoe_decoder *d, DevQ4 &m, const nmoe_tensor &t, int rows, int cols)
            dcopy(d, &m.b, t.biases, (size_t)rows * cols / 64 * 2);
 }
 
-cudaError_t matvec(const DevQ4 &m, const float *x, const float *resid, float *y, cudaStream_t st) {
-    const int blocks = (m.rows + kMvWarps - 1) / kMvWarps;
-    if (m.cols == 2048) k_q4_matvec<2048><<<blocks, kMvWarps * 32, 0, st>>>(m.w, m.s, m.b, m.rows, x, resid, y);
-    else k_q4_matvec<4096><<<blocks, kMvWarps * 32, 0, st>>>(m.w, m.s, m.b, m.rows, x, resid, y);
+// One launch of k_q4_matvec over n (<= 4) matrices of the same width; x normalised
+// first when norm_w is set (then the width is kHidden); resid only with n == 1.
+cudaError_t matvec(const DevQ4 *const *m, float *const *y, int n, const float *x, const uint16_t *norm_w,
+                   const float *resid, cudaStream_t st) {
+    MvArgs a{};
+    int rows = 0;
+    for (int i = 0; i < n; ++i) {
+        rows += m[i]->rows;
+        a.seg[i] = MvSeg{m[i]->w, m[i]->s, m[i]->b, y[i], rows};
+    }
+    a.nseg = n;
+    a.x = x;
+    a.resid = resid;
+    a.norm_w = norm_w;
+    const int blocks = (rows + kMvWarps - 1) / kMvWarps;
+    if (m[0]->cols == 2048) k_q4_matvec<2048><<<blocks, kMvWarps * 32, 0, st>>>(a);
+    else k_q4_matvec<4096><<<blocks, kMvWarps * 32, 0, st>>>(a);
     return cudaGetLastError();
+}
+
+cudaError_t matvec(const DevQ4 &m, const float *x, const float *resid, float *y, cudaStream_t st) {
+    const DevQ4 *mm[1] = {&m};
+    float *yy[1] = {y};
+    return matvec(mm, yy, 1, x, nullptr, resid, st);
 }
 
 }  // namespace
@@ -360,9 +423,9 @@ int enqueue_step(nmoe_decoder *d, const uint32_t *d_token, uint32_t *d_next, flo
     for (int l = 0; l < d->num_layers; ++l) {
         if (is_full(l)) {
             FullLayer &F = d->full[l];
-            k_rmsnorm<<<1, 256, 0, st>>>(h, F.in_norm, d->xn);
-            if (matvec(F.q, d->xn, nullptr, d->q, st) != cudaSuccess || matvec(F.k, d->xn, nullptr, d->kk, st) != cudaSuccess ||
-                matvec(F.v, d->xn, nullptr, d->vv, st) != cudaSuccess)
+            const DevQ4 *mm[3] = {&F.q, &F.k, &F.v};
+            float *yy[3] = {d->q, d->kk, d->vv};
+            if (matvec(mm, yy, 3, h, F.in_norm, nullptr, st) != cudaSuccess)
                 return dfail(d, NMOE_ECUDA, "layer %d projections", l);
             nmoe_full_attn_weights aw{F.q_norm, F.k_norm};
             int rc = nmoe::full_attn_step_dev(&aw, d->q, d->kk, d->vv, F.k_cache, F.v_cache, d->d_pos, d->attn,
@@ -372,10 +435,9 @@ int enqueue_step(nmoe_decoder *d, const uint32_t *d_token, uint32_t *d_next, flo
             k_rmsnorm<<<1, 256, 0, st>>>(d->h2, F.post_norm, d->xn);
         } else {
             LinearLayer &L = d->lin[l];
-            k_rmsnorm<<<1, 256, 0, st>>>(h, L.in_norm, d->xn);
-            if (matvec(L.qkv, d->xn, nullptr, d->qkv, st) != cudaSuccess || matvec(L.z, d->xn, nullptr, d->z, st) != cudaSuccess ||
-                matvec(L.beta, d->xn, nullptr, d->beta, st) != cudaSuccess ||
-                matvec(L.alpha, d->xn, nullptr, d->alpha, st) != cudaSuccess)
+            const DevQ4 *mm[4] = {&L.qkv, &L.z, &L.beta, &L.alpha};
+            float *yy[4] = {d->qkv, d->z, d->beta, d->alpha};
+            if (matvec(mm, yy, 4, h, L.in_norm, nullptr, st) != cudaSuccess)
                 return dfail(d, NMOE_ECUDA, "layer %d projections", l);
             nmoe_linear_attn_weights lw{L.conv_w, L.A_log, L.dt_bias, L.norm_w};
             int rc = nmoe_linear_attn_step(&lw, d->qkv, d->z, d->alpha, d->beta, L.conv_state, L.delta_state, d->attn,
