@@ -24,6 +24,10 @@ replica on its own GPU ("replicas only"), value = all ranks' layer calls / max t
 --workload batched (config 2): T tokens [T, 2048] bf16 through the MoE block of each
 of --layers resident layers per step (nmoe_moe_forward_batched: routing, expert-order
 permutation, tcgen05 grouped GEMMs with in-TMEM dequant, combine); value = tokens/s/layer.
+
+--workload decode_step (config 3): the whole 40-layer decode step (nmoe_decoder_step:
+embedding, attention layers with their q4 projections, MoE blocks, LM head), tokens/s;
+the default run (N = 1) adds it to its line as `decode_step`.
 """
 from __future__ import annotations
 
@@ -675,6 +679,13 @@ def run_ours(args, rank, world, local_rank):
         result["layer_crc32c"] = run_crc(args, dev)
         result["linear_attn"] = run_linear_attn(args, dev)
         result["full_attn"] = run_full_attn(args, dev)
+        if world == 1:   # config 3 beside the per-layer line: 60 graphed steps
+            try:
+                result["decode_step"] = run_decode_step(argparse.Namespace(**{**vars(args), "steps": 60,
+                                                                               "warmup": 5}), dev)
+            except Exception as e:   # reported, never fatal to the headline line
+                result["decode_step"] = {"error": f"{type(e).__name__}: {e}"}
+            torch.cuda.empty_cache()
     if args.ep_tokens > 0:
         ep = run_ep_batched(args, rank, world, dev)
         if result is not None:
