@@ -340,6 +340,21 @@ int nmoe_full_attn_step(const nmoe_full_attn_weights *w, const float *q, const f
                         int max_positions, float *out, void *workspace, void *stream);
 size_t nmoe_full_attn_workspace_bytes(void);
 
+/* The same step for a batch of sequences over a bf16 KV cache (batch 64
+ * at 32k context; the reference's cache is f32 and batch 1). DEVICE pointers: q f32
+ * [batch][16][512], k_new / v_new f32 [batch][2][256], k_cache / v_cache bf16
+ * [batch][max_positions][2][256] (sequence b's row d_positions[b] is written, rounded to
+ * nearest even), d_positions int32 [batch] read on the device (a position outside
+ * [0, max_positions) leaves that sequence's caches untouched and its out zero), out f32
+ * [batch][16][256]. workspace: nmoe_full_attn_batched_workspace_bytes(batch), 16-byte
+ * aligned. Two launches of batch x 148 and batch x 16 CTAs; allocates nothing;
+ * capturable (positions on the device: one graph serves every step). */
+int nmoe_full_attn_step_batched(const nmoe_full_attn_weights *w, int batch, const float *q,
+                                const float *k_new, const float *v_new, uint16_t *k_cache,
+                                uint16_t *v_cache, const int32_t *d_positions, int max_positions,
+                                float *out, void *workspace, void *stream);
+size_t nmoe_full_attn_batched_workspace_bytes(int batch);
+
 /* ---- Whole decode step ------------------------------------------
  * The C restatement of NMOEProcessToken (src/runtime.m:3712-3805) on the GPU: embedding
  * row, 40 layers (layer l is full attention when (l + 1) % 4 == 0, else linear attention:

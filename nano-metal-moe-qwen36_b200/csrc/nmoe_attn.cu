@@ -33,11 +33,13 @@ constexpr float kTheta = 10000000.0f;
 struct FaArgs {
     const float *q, *k_new, *v_new;
     const uint16_t *q_norm, *k_norm;
-    float *k_cache, *v_cache, *out;
-    float *part;          // [kKV][kMaxSplit][kGroup][kPart]
-    int position, splits;
-    const int *d_position;   // when set: the position is read on the device (graph replays) and
-                             // the grid holds kMaxSplit slices per KV head, the unused ones exit
+    void *k_cache, *v_cache;   // f32 or bf16 [batch][cap][2][256]
+    float *out;
+    float *part;          // [batch][kKV][kMaxSplit][kGroup][kPart]
+    int position, splits, cap;
+    const int *d_position;   // when set: sequence b's position is d_position[b], read on the device
+                             // (graph replays, batches), and the grid holds kMaxSplit slices per
+                             // KV head, the unused ones exit
     float freq[32];       // RoPE frequencies theta^(-2t/64), correctly rounded to float
 };
 
@@ -48,6 +50,15 @@ __host__ __device__ __forceinline__ int slices_for(int position) {
 }
 
 __device__ __forceinline__ float bf16f(uint16_t v) { return __uint_as_float((uint32_t)v << 16); }
+
+// cache elements: f32 (the reference's cache) or bf16 (uint16_t, round to nearest even)
+__device__ __forceinline__ float kv_load(const float *p) { return __ldcs(p); }
+__device__ __forceinline__ float kv_load(const uint16_t *p) { return bf16f(__ldcs(reinterpret_cast<const unsigned short *>(p))); }
+__device__ __forceinline__ void kv_store(float *p, float v) { *p = v; }
+__device__ __forceinline__ void kv_store(uint16_t *p, float v) {
+    const uint32_t u = __float_as_uint(v);
+    *p = (uint16_t)((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
+}
 
 // RMS norm (eps 1e-6, weight + 1) and rotate-half RoPE of one 256-vector held by a warp,
 // lane l: dims l + 32 j (kernels.metal:1006-1053).
@@ -71,6 +82,7 @@ __device__ __forceinline__ void prep_vec(float *v, const uint16_t *w, int positi
     v[1] = v0 * s + v1 * c;
 }
 
+template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) k_full_attn_step(const FaArgs a) {
     extern __shared__ float smf[];
     float *qs = smf;                             // [8][256] prepared queries
@@ -79,7 +91,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_full_attn_step(const FaArgs a) 
     float *tl = tm + kWarps * kGroup;            // [8 warps][8 heads]
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int position = a.d_position ? *a.d_position : a.position;
+    const int b = blockIdx.y;   // sequence
+    const int position = a.d_position ? a.d_position[b] : a.position;
+    if (position < 0 || position >= a.cap) return;   // the merge writes zeros for it
+    const float *Q = a.q + (size_t)b * kHeads * 2 * kDim;
+    const float *KN = a.k_new + (size_t)b * kKV * kDim, *VN = a.v_new + (size_t)b * kKV * kDim;
+    T *KC = static_cast<T *>(a.k_cache) + (size_t)b * a.cap * kKV * kDim;
+    T *VC = static_cast<T *>(a.v_cache) + (size_t)b * a.cap * kKV * kDim;
     const int splits = a.d_position ? slices_for(position) : a.splits;
     const int grid_splits = a.d_position ? kMaxSplit : a.splits;
     const int kvh = blockIdx.x / grid_splits, split = blockIdx.x % grid_splits;
@@ -94,7 +112,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_full_attn_step(const FaArgs a) 
         const int h = kGroup * kvh + warp;
         float v[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = a.q[h * 2 * kDim + lane + 32 * j];
+        for (int j = 0; j < 8; ++j) v[j] = Q[h * 2 * kDim + lane + 32 * j];
         prep_vec(v, a.q_norm, position, lane, a.freq);
 #pragma unroll
         for (int j = 0; j < 8; ++j) qs[warp * kDim + lane + 32 * j] = v[j];
@@ -103,13 +121,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_full_attn_step(const FaArgs a) 
     if (holds_new && warp == 0) {
         float v[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = a.k_new[kvh * kDim + lane + 32 * j];
+        for (int j = 0; j < 8; ++j) v[j] = KN[kvh * kDim + lane + 32 * j];
         prep_vec(v, a.k_norm, position, lane, a.freq);
         const size_t row = ((size_t)position * kKV + kvh) * kDim;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            a.k_cache[row + lane + 32 * j] = v[j];
-            a.v_cache[row + lane + 32 * j] = a.v_new[kvh * kDim + lane + 32 * j];
+            kv_store(KC + row + lane + 32 * j, v[j]);
+            kv_store(VC + row + lane + 32 * j, VN[kvh * kDim + lane + 32 * j]);
         }
     }
     __syncthreads();
@@ -133,12 +151,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_full_attn_step(const FaArgs a) 
     float kr[8], vr[8], k1[8], v1[8], k2[8], v2[8];
     auto load_row = [&](int p, float *kx, float *vx) {
         if (p < p1) {
-            const float *kp = a.k_cache + ((size_t)p * kKV + kvh) * kDim;
-            const float *vp = a.v_cache + ((size_t)p * kKV + kvh) * kDim;
+            const T *kp = KC + ((size_t)p * kKV + kvh) * kDim;
+            const T *vp = VC + ((size_t)p * kKV + kvh) * kDim;
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
-                kx[j] = __ldcs(kp + lane + 32 * j);
-                vx[j] = __ldcs(vp + lane + 32 * j);
+                kx[j] = kv_load(kp + lane + 32 * j);
+                vx[j] = kv_load(vp + lane + 32 * j);
             }
         }
     };
@@ -189,7 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_full_attn_step(const FaArgs a) 
     __syncthreads();
     {
         const int d = tid;   // one dim per thread, all 8 heads
-        float *pb = a.part + ((size_t)kvh * kMaxSplit + split) * kGroup * kPart;
+        float *pb = a.part + (((size_t)b * kKV + kvh) * kMaxSplit + split) * kGroup * kPart;
 #pragma unroll 1
         for (int h = 0; h < kGroup; ++h) {
             float M = -1e30f;
@@ -216,9 +234,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_full_attn_step(const FaArgs a) 
 __global__ void __launch_bounds__(kThreads) k_full_attn_merge(const FaArgs a) {
     __shared__ float sm_m[kMaxSplit], sm_l[kMaxSplit];
     const int tid = threadIdx.x;
-    const int splits = a.d_position ? slices_for(*a.d_position) : a.splits;
+    const int b = blockIdx.y;   // sequence
+    const int position = a.d_position ? a.d_position[b] : a.position;
     const int kvh = blockIdx.x / kGroup, h = blockIdx.x % kGroup;
-    const float *pb = a.part + (size_t)kvh * kMaxSplit * kGroup * kPart + (size_t)h * kPart;
+    const int hq = kGroup * kvh + h;
+    float *out = a.out + (size_t)b * kHeads * kDim;
+    if (position < 0 || position >= a.cap) {   // a position outside the cache: zeros
+        out[hq * kDim + tid] = 0.f;
+        return;
+    }
+    const int splits = a.d_position ? slices_for(position) : a.splits;
+    const float *pb = a.part + ((size_t)b * kKV + kvh) * kMaxSplit * kGroup * kPart + (size_t)h * kPart;
     const size_t sstride = (size_t)kGroup * kPart;
     if (tid < splits) {
         sm_m[tid] = pb[tid * sstride + kDim];
@@ -234,9 +260,8 @@ __global__ void __launch_bounds__(kThreads) k_full_attn_merge(const FaArgs a) {
         L = fmaf(sm_l[sI], e, L);
         A = fmaf(pb[sI * sstride + tid], e, A);
     }
-    const int hq = kGroup * kvh + h;
-    const float gate = 1.0f / (1.0f + expf(-a.q[hq * 2 * kDim + kDim + tid]));
-    a.out[hq * kDim + tid] = (L > 0.f ? A / L : 0.f) * gate;
+    const float gate = 1.0f / (1.0f + expf(-a.q[(size_t)b * kHeads * 2 * kDim + hq * 2 * kDim + kDim + tid]));
+    out[hq * kDim + tid] = (L > 0.f ? A / L : 0.f) * gate;
 }
 
 constexpr size_t kSmem = (size_t)(kGroup * kDim + kWarps * kGroup * kDim + 2 * kWarps * kGroup) * 4;
@@ -247,14 +272,19 @@ extern "C" size_t nmoe_full_attn_workspace_bytes(void) {
     return (size_t)kKV * kMaxSplit * kGroup * kPart * 4 + 256;
 }
 
+extern "C" size_t nmoe_full_attn_batched_workspace_bytes(int batch) {
+    return batch < 1 ? 0 : (size_t)batch * kKV * kMaxSplit * kGroup * kPart * 4 + 256;
+}
+
 namespace {
 
-int launch_full_attn(const nmoe_full_attn_weights *w, const float *q, const float *k_new, const float *v_new,
-                     float *k_cache, float *v_cache, int position, const int *d_position, float *out,
-                     void *workspace, cudaStream_t st) {
-    static bool attr_set = false;   // per process; the attribute is a function property
+template <typename T>
+int launch_full_attn(const nmoe_full_attn_weights *w, int batch, const float *q, const float *k_new,
+                     const float *v_new, T *k_cache, T *v_cache, int cap, int position, const int *d_position,
+                     float *out, void *workspace, cudaStream_t st) {
+    static bool attr_set = false;   // per process and element type; a function property
     if (!attr_set) {
-        if (cudaFuncSetAttribute(k_full_attn_step, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem) !=
+        if (cudaFuncSetAttribute(k_full_attn_step<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem) !=
             cudaSuccess)
             return NMOE_ECUDA;
         attr_set = true;
@@ -271,11 +301,12 @@ int launch_full_attn(const nmoe_full_attn_weights *w, const float *q, const floa
     a.part = static_cast<float *>(workspace);
     a.position = position;
     a.splits = slices_for(position);
+    a.cap = cap;
     a.d_position = d_position;
     for (int t = 0; t < 32; ++t) a.freq[t] = (float)pow((double)kTheta, -2.0 * t / 64.0);
-    const int grid = kKV * (d_position ? kMaxSplit : a.splits);
-    k_full_attn_step<<<grid, kThreads, kSmem, st>>>(a);
-    k_full_attn_merge<<<kKV * kGroup, kThreads, 0, st>>>(a);
+    const dim3 grid(kKV * (d_position ? kMaxSplit : a.splits), batch);
+    k_full_attn_step<T><<<grid, kThreads, kSmem, st>>>(a);
+    k_full_attn_merge<<<dim3(kKV * kGroup, batch), kThreads, 0, st>>>(a);
     return cudaGetLastError() == cudaSuccess ? NMOE_OK : NMOE_ECUDA;
 }
 
@@ -289,8 +320,22 @@ extern "C" int nmoe_full_attn_step(const nmoe_full_attn_weights *w, const float 
         return NMOE_EINVAL;
     if (position < 0 || position >= max_positions) return NMOE_EINVAL;
     if ((reinterpret_cast<uintptr_t>(workspace) & 15u) != 0) return NMOE_EINVAL;
-    return launch_full_attn(w, q, k_new, v_new, k_cache, v_cache, position, nullptr, out, workspace,
-                            static_cast<cudaStream_t>(stream));
+    return launch_full_attn<float>(w, 1, q, k_new, v_new, k_cache, v_cache, max_positions, position, nullptr, out,
+                                   workspace, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int nmoe_full_attn_step_batched(const nmoe_full_attn_weights *w, int batch, const float *q,
+                                           const float *k_new, const float *v_new, uint16_t *k_cache,
+                                           uint16_t *v_cache, const int32_t *d_positions, int max_positions,
+                                           float *out, void *workspace, void *stream) {
+    if (w == nullptr || w->q_norm == nullptr || w->k_norm == nullptr || q == nullptr || k_new == nullptr ||
+        v_new == nullptr || k_cache == nullptr || v_cache == nullptr || d_positions == nullptr || out == nullptr ||
+        workspace == nullptr)
+        return NMOE_EINVAL;
+    if (batch < 1 || batch > 65535 || max_positions < 1) return NMOE_EINVAL;
+    if ((reinterpret_cast<uintptr_t>(workspace) & 15u) != 0) return NMOE_EINVAL;
+    return launch_full_attn<uint16_t>(w, batch, q, k_new, v_new, k_cache, v_cache, max_positions, 0, d_positions,
+                                      out, workspace, static_cast<cudaStream_t>(stream));
 }
 
 namespace nmoe {
@@ -298,8 +343,9 @@ namespace nmoe {
 // caller to lie in [0, max_positions)): one launch shape for every position, so that a
 // captured graph of decode steps replays at any position.
 int full_attn_step_dev(const nmoe_full_attn_weights *w, const float *q, const float *k_new, const float *v_new,
-                       float *k_cache, float *v_cache, const int *d_position, float *out, void *workspace,
-                       cudaStream_t st) {
-    return launch_full_attn(w, q, k_new, v_new, k_cache, v_cache, 0, d_position, out, workspace, st);
+                       float *k_cache, float *v_cache, int max_positions, const int *d_position, float *out,
+                       void *workspace, cudaStream_t st) {
+    return launch_full_attn<float>(w, 1, q, k_new, v_new, k_cache, v_cache, max_positions, 0, d_position, out,
+                                   workspace, st);
 }
 }  // namespace nmoe

@@ -23,8 +23,8 @@
 
 namespace nmoe {
 int full_attn_step_dev(const nmoe_full_attn_weights *w, const float *q, const float *k_new, const float *v_new,
-                       float *k_cache, float *v_cache, const int *d_position, float *out, void *workspace,
-                       cudaStream_t st);
+                       float *k_cache, float *v_cache, int max_positions, const int *d_position, float *out,
+                       void *workspace, cudaStream_t st);
 }
 
 namespace {
@@ -428,7 +428,7 @@ int enqueue_step(nmoe_decoder *d, const uint32_t *d_token, uint32_t *d_next, flo
             if (matvec(mm, yy, 3, h, F.in_norm, nullptr, st) != cudaSuccess)
                 return dfail(d, NMOE_ECUDA, "layer %d projections", l);
             nmoe_full_attn_weights aw{F.q_norm, F.k_norm};
-            int rc = nmoe::full_attn_step_dev(&aw, d->q, d->kk, d->vv, F.k_cache, F.v_cache, d->d_pos, d->attn,
+            int rc = nmoe::full_attn_step_dev(&aw, d->q, d->kk, d->vv, F.k_cache, F.v_cache, d->max_pos, d->d_pos, d->attn,
                                               d->fa_ws, st);
             if (rc != NMOE_OK) return dfail(d, rc, "layer %d attention", l);
             if (matvec(F.o, d->attn, h, d->h2, st) != cudaSuccess) return dfail(d, NMOE_ECUDA, "layer %d o_proj", l);

@@ -34,6 +34,7 @@ ABI_SYMBOLS = (
     "nmoe_lm_head_argmax", "nmoe_lm_head_workspace_bytes", "nmoe_lm_head_error",
     "nmoe_moe_load_layer_checked", "nmoe_moe_load_layer_file_checked", "nmoe_crc32c", "nmoe_crc32c_combine",
     "nmoe_crc32c_device", "nmoe_linear_attn_step", "nmoe_full_attn_step", "nmoe_full_attn_workspace_bytes",
+    "nmoe_full_attn_step_batched", "nmoe_full_attn_batched_workspace_bytes",
     "nmoe_decoder_create", "nmoe_decoder_destroy", "nmoe_decoder_error", "nmoe_decoder_set_linear_layer",
     "nmoe_decoder_set_full_layer", "nmoe_decoder_set_globals", "nmoe_decoder_reset", "nmoe_decoder_step",
 )
@@ -163,6 +164,10 @@ def lib() -> C.CDLL:
     L.nmoe_full_attn_step.restype = i
     L.nmoe_full_attn_step.argtypes = [C.POINTER(FullAttnWeights), vp, vp, vp, vp, vp, i, i, vp, vp, vp]
     L.nmoe_full_attn_workspace_bytes.restype = sz
+    L.nmoe_full_attn_step_batched.restype = i
+    L.nmoe_full_attn_step_batched.argtypes = [C.POINTER(FullAttnWeights), i, vp, vp, vp, vp, vp, vp, i, vp, vp, vp]
+    L.nmoe_full_attn_batched_workspace_bytes.restype = sz
+    L.nmoe_full_attn_batched_workspace_bytes.argtypes = [i]
     L.nmoe_decoder_create.restype = vp
     L.nmoe_decoder_create.argtypes = [vp, i, i, i, C.POINTER(i)]
     L.nmoe_decoder_destroy.argtypes = [vp]
@@ -502,6 +507,23 @@ def full_attn_step(weights: dict, q, k_new, v_new, k_cache, v_cache, position: i
                                    position, max_positions, _ptr(out), _ptr(workspace), stream)
     if rc != OK:
         raise NmoeError(rc, "nmoe_full_attn_step")
+
+
+def full_attn_batched_workspace_bytes(batch: int) -> int:
+    return int(lib().nmoe_full_attn_batched_workspace_bytes(batch))
+
+
+def full_attn_step_batched(weights: dict, q, k_new, v_new, k_cache, v_cache, positions, max_positions: int, out,
+                           workspace, stream=0):
+    """nmoe_full_attn_step_batched: the step for a batch of sequences over bf16 caches
+    (device tensors; caches int16/bf16 [B][max_positions][2][256], positions int32 [B] on
+    the device)."""
+    w = FullAttnWeights(_ptr(weights["q_norm"]), _ptr(weights["k_norm"]))
+    rc = lib().nmoe_full_attn_step_batched(C.byref(w), int(q.shape[0]), _ptr(q), _ptr(k_new), _ptr(v_new),
+                                           _ptr(k_cache), _ptr(v_cache), _ptr(positions), max_positions, _ptr(out),
+                                           _ptr(workspace), stream)
+    if rc != OK:
+        raise NmoeError(rc, "nmoe_full_attn_step_batched")
 
 
 def _q4t(m):

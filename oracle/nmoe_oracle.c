@@ -600,14 +600,20 @@ static void orc_fa_prep(float *vec, const uint16_t *w, int position) {
     }
 }
 
-void orc_full_attn_step(const float *q, const float *k_new, const float *v_new, const uint16_t *q_norm,
-                        const uint16_t *k_norm, float *k_cache, float *v_cache, int position, float *out) {
+static void fa_step(const float *q, const float *k_new, const float *v_new, const uint16_t *q_norm,
+                    const uint16_t *k_norm, float *k_cache, float *v_cache, int position, float *out, int bf16_kv) {
     for (int kh = 0; kh < 2; kh++) {
-        float kv[256];
+        float kv[256], vv[256];
         memcpy(kv, k_new + kh * 256, sizeof kv);
+        memcpy(vv, v_new + kh * 256, sizeof vv);
         orc_fa_prep(kv, k_norm, position);
+        if (bf16_kv)   /* the rows as a bf16 cache stores them (round to nearest even) */
+            for (int i = 0; i < 256; i++) {
+                kv[i] = orc_bf16_to_f32(orc_f32_to_bf16(kv[i]));
+                vv[i] = orc_bf16_to_f32(orc_f32_to_bf16(vv[i]));
+            }
         memcpy(k_cache + ((size_t)position * 2 + kh) * 256, kv, sizeof kv);
-        memcpy(v_cache + ((size_t)position * 2 + kh) * 256, v_new + kh * 256, sizeof kv);
+        memcpy(v_cache + ((size_t)position * 2 + kh) * 256, vv, sizeof vv);
     }
     const int seq = position + 1;
     float *sc = (float *)malloc((size_t)seq * sizeof(float));
@@ -633,4 +639,14 @@ void orc_full_attn_step(const float *q, const float *k_new, const float *v_new, 
         }
     }
     free(sc);
+}
+
+void orc_full_attn_step(const float *q, const float *k_new, const float *v_new, const uint16_t *q_norm,
+                        const uint16_t *k_norm, float *k_cache, float *v_cache, int position, float *out) {
+    fa_step(q, k_new, v_new, q_norm, k_norm, k_cache, v_cache, position, out, 0);
+}
+
+void orc_full_attn_step_bf16kv(const float *q, const float *k_new, const float *v_new, const uint16_t *q_norm,
+                               const uint16_t *k_norm, float *k_cache, float *v_cache, int position, float *out) {
+    fa_step(q, k_new, v_new, q_norm, k_norm, k_cache, v_cache, position, out, 1);
 }

@@ -167,6 +167,11 @@ void orc_linear_attn_step(const float *qkv, const float *z, const float *alpha, 
  * [256]; caches updated at `position`; out f32 [16][256]. q is not modified. */
 void orc_full_attn_step(const float *q, const float *k_new, const float *v_new, const uint16_t *q_norm,
                         const uint16_t *k_norm, float *k_cache, float *v_cache, int position, float *out);
+/* The same step over a bf16 KV cache (the reference's cache is f32):
+ * the caches are f32 arrays holding bf16 values, and the appended k (after norm and RoPE)
+ * and v rows are rounded to bf16 (nearest even) before the attention reads them. */
+void orc_full_attn_step_bf16kv(const float *q, const float *k_new, const float *v_new, const uint16_t *q_norm,
+                               const uint16_t *k_norm, float *k_cache, float *v_cache, int position, float *out);
 
 /* Set the OpenMP thread count used by the matvecs (0 = library default). */
 void orc_set_threads(int n);

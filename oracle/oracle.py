@@ -93,6 +93,7 @@ def lib() -> C.CDLL:
         L.orc_linear_attn_step.argtypes = [_f32p, _f32p, _f32p, _f32p, _u16p, _f32p, _u16p, _u16p, _f32p, _f32p,
                                            _f32p]
         L.orc_full_attn_step.argtypes = [_f32p, _f32p, _f32p, _u16p, _u16p, _f32p, _f32p, C.c_int, _f32p]
+        L.orc_full_attn_step_bf16kv.argtypes = L.orc_full_attn_step.argtypes
         L.orc_set_threads.argtypes = [C.c_int]
         L.orc_get_threads.restype = C.c_int
         _lib = L
@@ -371,10 +372,12 @@ def linear_attn_step(w, inp, conv_state, delta_state):
     return out
 
 
-def full_attn_step(q, k_new, v_new, q_norm, k_norm, k_cache, v_cache, position):
-    """One full-attention decode step by the reference's sequence; caches updated."""
+def full_attn_step(q, k_new, v_new, q_norm, k_norm, k_cache, v_cache, position, bf16_kv: bool = False):
+    """One full-attention decode step by the reference's sequence; caches updated. bf16_kv:
+    the caches hold bf16 values (f32 arrays) and the appended rows are rounded to bf16."""
     out = np.zeros(16 * 256, np.float32)
-    lib().orc_full_attn_step(np.ascontiguousarray(q, np.float32).reshape(-1), k_new.reshape(-1), v_new.reshape(-1),
+    fn = lib().orc_full_attn_step_bf16kv if bf16_kv else lib().orc_full_attn_step
+    fn(np.ascontiguousarray(q, np.float32).reshape(-1), k_new.reshape(-1), v_new.reshape(-1),
                              q_norm, k_norm, k_cache.reshape(-1), v_cache.reshape(-1), int(position), out)
     return out
 
