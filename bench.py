@@ -927,6 +927,53 @@ def run_full_attn(args, dev):
     return res
 
 
+def run_full_attn_batched(args, dev):
+    """Config 4's attention: nmoe_full_attn_step_batched for 64 sequences at position 32767
+    over one layer's bf16 caches (64 x 32768 x 2 x 256 x 2 bytes each for K and V: 4.3 GB),
+    device time per call (CUDA graph of 5 calls x 3 replays); bytes = the K and V rows read
+    plus the new rows, against HBM."""
+    import torch
+    import nmoe_b200 as N
+    from oracle import oracle as O
+    B, cap = 64, 32768
+    pos = cap - 1
+    rng = np.random.default_rng(args.seed + 23)
+    w = {"q_norm": O.randn_bf16(rng, (256,), 0.1), "k_norm": O.randn_bf16(rng, (256,), 0.1)}
+    dw = {k: torch.from_numpy(v.view(np.int16).copy()).to(f"cuda:{dev}") for k, v in w.items()}
+    ws = torch.zeros(N.full_attn_batched_workspace_bytes(B) // 4, dtype=torch.int32, device=f"cuda:{dev}")
+    q = torch.randn(B, 16, 512, device=f"cuda:{dev}")
+    kn = torch.randn(B, 2, 256, device=f"cuda:{dev}")
+    vn = torch.randn(B, 2, 256, device=f"cuda:{dev}")
+    out = torch.zeros(B, 16 * 256, device=f"cuda:{dev}")
+    kc = (torch.randn(B, cap, 2, 256, device=f"cuda:{dev}") * 0.3).to(torch.bfloat16)
+    vc = torch.randn(B, cap, 2, 256, device=f"cuda:{dev}").to(torch.bfloat16)
+    positions = torch.full((B,), pos, dtype=torch.int32, device=f"cuda:{dev}")
+    st = torch.cuda.Stream(device=dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=st):
+        for _ in range(5):
+            N.full_attn_step_batched(dw, q, kn, vn, kc, vc, positions, cap, out, ws,
+                                     stream=torch.cuda.current_stream().cuda_stream)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    with torch.cuda.stream(st):
+        for _ in range(3):
+            g.replay()
+    e1.record(st)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / 15
+    pk, pk_kind = peaks()
+    ab = B * ((pos + 1) * 2 * 256 * 2 * 2 + 16 * 512 * 4 + 16 * 256 * 4)
+    ach = ab / (us * 1e-6) / 1e9
+    return {"batch": B, "position": pos, "us_per_call": us, "sequences_per_s": B / (us * 1e-6),
+            "roofline": {"bound": "hbm", "achieved": ach, "peak": pk, "unit": "GB/s", "frac": ach / pk,
+                         "peak_kind": pk_kind, "algorithmic_bytes_per_launch": ab},
+            "l2": "4.3 GB of K and V per call: far above L2"}
+
+
 def fast_decoder_weights(seed: int, num_layers: int, vocab: int):
     """Synthetic q4 attention / embedding / head weights of the 40-layer model, drawn
     directly in the packed format (uniform nibbles, scale 0.005, bias -0.0375: weights
@@ -1086,7 +1133,7 @@ def main():
     ap.add_argument("--pool", type=int, default=32, help="distinct expert packs generated on the host")
     ap.add_argument("--seed", type=int, default=2026)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--workload", choices=["decode", "batched", "lm_head", "crc", "linear_attn", "full_attn", "decode_step"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "batched", "lm_head", "crc", "linear_attn", "full_attn", "decode_step", "full_attn_batched"], default="decode")
     ap.add_argument("--lm-dtypes", default="q4,bf16", help="LM head weight types timed (q4, bf16)")
     ap.add_argument("--bits", type=int, choices=[2, 4], default=4, help="decode: expert packs (4: config 0, 2: config 1)")
     ap.add_argument("--k", type=int, default=8, help="decode: routed experts per token (config 1 sweeps 1..8)")
@@ -1119,7 +1166,11 @@ def main():
         import torch.distributed as dist
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local_rank}"))
-    if args.workload == "decode_step":
+    if args.workload == "full_attn_batched":
+        import torch
+        torch.cuda.set_device(local_rank)
+        res = {"workload": "full_attn_batched", **run_full_attn_batched(args, local_rank)} if rank == 0 else None
+    elif args.workload == "decode_step":
         import torch
         torch.cuda.set_device(local_rank)
         res = {"workload": "decode_step", **run_decode_step(args, local_rank)} if rank == 0 else None
