@@ -318,6 +318,13 @@ typedef struct nmoe_linear_attn_weights {
 int nmoe_linear_attn_step(const nmoe_linear_attn_weights *w, const float *qkv, const float *z,
                           const float *alpha, const float *beta, float *conv_state, float *delta_state,
                           float *out, void *stream);
+/* The same step for a batch of sequences, one launch of batch x 128
+ * CTAs: every pointer covers `batch` consecutive copies of the single-sequence layout
+ * (qkv [batch][8192], z [batch][4096], alpha / beta [batch][32], conv_state
+ * [batch][3][8192], delta_state [batch][32][128][128], out [batch][4096]). */
+int nmoe_linear_attn_step_batched(const nmoe_linear_attn_weights *w, int batch, const float *qkv,
+                                  const float *z, const float *alpha, const float *beta,
+                                  float *conv_state, float *delta_state, float *out, void *stream);
 
 /* ---- Full-attention decode step --------------------------------------------------
  * Replaces, in NMOEFullAttentionStepMetal (src/runtime.m:3040-3095), nmoe_full_qk_prep

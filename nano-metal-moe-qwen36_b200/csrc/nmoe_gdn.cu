@@ -57,12 +57,17 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1) 
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int r = (int)cluster.block_rank();
+    // sequence blockIdx.y of a batch: its inputs, states and output
+    const size_t sq = blockIdx.y;
+    const float *qkv = a.qkv + sq * kConv, *zin = a.z + sq * kVH * kD;
+    const float *alpha = a.alpha + sq * kVH, *beta = a.beta + sq * kVH;
+    float *conv_state = a.conv_state + sq * 3 * kConv, *out = a.out + sq * kVH * kD;
     const int kh = blockIdx.x / kCluster;
     const int vh = 2 * kh + (r >> 2), split = r & 3;
 
     // the 32 state rows are issued first: their HBM latency overlaps the conv, the
     // exchanges and the norms (warp w rows 8w..8w+7, lane l keys 4l..4l+3)
-    float4 *S = reinterpret_cast<float4 *>(a.delta_state + ((size_t)vh * kD + kRows * split + 8 * warp) * kD);
+    float4 *S = reinterpret_cast<float4 *>(a.delta_state + sq * kVH * kD * kD + ((size_t)vh * kD + kRows * split + 8 * warp) * kD);
     float4 st[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) st[i] = __ldcs(S + i * (kD / 4) + lane);
@@ -74,17 +79,17 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1) 
         else if (tid < 32) ch = 2048 + kh * kD + 16 * r + (tid - 16);        // k
         else ch = 4096 + vh * kD + kRows * split + (tid - 32);               // v
         const uint2 wv = *reinterpret_cast<const uint2 *>(a.conv_w + 4 * ch);
-        const float s0 = a.conv_state[ch], s1 = a.conv_state[kConv + ch], s2 = a.conv_state[2 * kConv + ch];
-        const float inp = a.qkv[ch];
+        const float s0 = conv_state[ch], s1 = conv_state[kConv + ch], s2 = conv_state[2 * kConv + ch];
+        const float inp = qkv[ch];
         float acc = 0.0f;
         acc += s0 * bf16f((uint16_t)(wv.x & 0xFFFFu));
         acc += s1 * bf16f((uint16_t)(wv.x >> 16));
         acc += s2 * bf16f((uint16_t)(wv.y & 0xFFFFu));
         acc += inp * bf16f((uint16_t)(wv.y >> 16));
         const float c = silu(acc);
-        a.conv_state[ch] = s1;
-        a.conv_state[kConv + ch] = s2;
-        a.conv_state[2 * kConv + ch] = inp;
+        conv_state[ch] = s1;
+        conv_state[kConv + ch] = s2;
+        conv_state[2 * kConv + ch] = inp;
         if (tid < 32) qk_part[tid] = c;
         else vloc[tid - 32] = c;
     }
@@ -114,9 +119,9 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1) 
     __syncthreads();
     // ---- decay and beta of the value head (kernels.metal:1823-1839)
     const float A = expf(a.A_log[vh]);
-    const float sp = logf(1.0f + expf(a.alpha[vh] + bf16f(a.dt_bias[vh])));
+    const float sp = logf(1.0f + expf(alpha[vh] + bf16f(a.dt_bias[vh])));
     const float g = expf(-A * sp);
-    const float b = sigm(a.beta[vh]);
+    const float b = sigm(beta[vh]);
     // ---- delta rule on the 32 state rows (kernels.metal:1300-1346)
     {
         const float4 k4 = reinterpret_cast<const float4 *>(ks)[lane];
@@ -171,9 +176,27 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1) 
         for (int j = 0; j < 4; ++j) tot += *cluster.map_shared_rank(&ss_part, base + j);
         const float inv = rsqrtf(tot / (float)kD + 1e-6f);
         const int vi = kRows * split + tid;
-        a.out[vh * kD + vi] = oloc[tid] * inv * silu(a.z[vh * kD + vi]) * bf16f(a.norm_w[vi]);
+        out[vh * kD + vi] = oloc[tid] * inv * silu(zin[vh * kD + vi]) * bf16f(a.norm_w[vi]);
     }
     cluster.sync();   // no CTA leaves while another still reads its shared memory
+}
+
+}  // namespace
+
+namespace {
+
+int launch_gdn(const nmoe_linear_attn_weights *w, int batch, const float *qkv, const float *z, const float *alpha,
+               const float *beta, float *conv_state, float *delta_state, float *out, void *stream) {
+    if (w == nullptr || w->conv_w == nullptr || w->A_log == nullptr || w->dt_bias == nullptr ||
+        w->norm_w == nullptr || qkv == nullptr || z == nullptr || alpha == nullptr || beta == nullptr ||
+        conv_state == nullptr || delta_state == nullptr || out == nullptr)
+        return NMOE_EINVAL;
+    if (batch < 1 || batch > 65535) return NMOE_EINVAL;
+    if ((reinterpret_cast<uintptr_t>(delta_state) & 15u) != 0 || (reinterpret_cast<uintptr_t>(w->conv_w) & 7u) != 0)
+        return NMOE_EINVAL;
+    GdnArgs a{qkv, z, alpha, beta, w->conv_w, w->dt_bias, w->norm_w, w->A_log, conv_state, delta_state, out};
+    k_linear_attn_step<<<dim3(kKH * kCluster, batch), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
+    return cudaGetLastError() == cudaSuccess ? NMOE_OK : NMOE_ECUDA;
 }
 
 }  // namespace
@@ -181,13 +204,11 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 1) 
 extern "C" int nmoe_linear_attn_step(const nmoe_linear_attn_weights *w, const float *qkv, const float *z,
                                      const float *alpha, const float *beta, float *conv_state, float *delta_state,
                                      float *out, void *stream) {
-    if (w == nullptr || w->conv_w == nullptr || w->A_log == nullptr || w->dt_bias == nullptr ||
-        w->norm_w == nullptr || qkv == nullptr || z == nullptr || alpha == nullptr || beta == nullptr ||
-        conv_state == nullptr || delta_state == nullptr || out == nullptr)
-        return NMOE_EINVAL;
-    if ((reinterpret_cast<uintptr_t>(delta_state) & 15u) != 0 || (reinterpret_cast<uintptr_t>(w->conv_w) & 7u) != 0)
-        return NMOE_EINVAL;
-    GdnArgs a{qkv, z, alpha, beta, w->conv_w, w->dt_bias, w->norm_w, w->A_log, conv_state, delta_state, out};
-    k_linear_attn_step<<<kKH * kCluster, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
-    return cudaGetLastError() == cudaSuccess ? NMOE_OK : NMOE_ECUDA;
+    return launch_gdn(w, 1, qkv, z, alpha, beta, conv_state, delta_state, out, stream);
+}
+
+extern "C" int nmoe_linear_attn_step_batched(const nmoe_linear_attn_weights *w, int batch, const float *qkv,
+                                             const float *z, const float *alpha, const float *beta,
+                                             float *conv_state, float *delta_state, float *out, void *stream) {
+    return launch_gdn(w, batch, qkv, z, alpha, beta, conv_state, delta_state, out, stream);
 }

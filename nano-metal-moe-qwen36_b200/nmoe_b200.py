@@ -34,7 +34,7 @@ ABI_SYMBOLS = (
     "nmoe_lm_head_argmax", "nmoe_lm_head_workspace_bytes", "nmoe_lm_head_error",
     "nmoe_moe_load_layer_checked", "nmoe_moe_load_layer_file_checked", "nmoe_crc32c", "nmoe_crc32c_combine",
     "nmoe_crc32c_device", "nmoe_linear_attn_step", "nmoe_full_attn_step", "nmoe_full_attn_workspace_bytes",
-    "nmoe_full_attn_step_batched", "nmoe_full_attn_batched_workspace_bytes",
+    "nmoe_full_attn_step_batched", "nmoe_linear_attn_step_batched", "nmoe_full_attn_batched_workspace_bytes",
     "nmoe_decoder_create", "nmoe_decoder_destroy", "nmoe_decoder_error", "nmoe_decoder_set_linear_layer",
     "nmoe_decoder_set_full_layer", "nmoe_decoder_set_globals", "nmoe_decoder_reset", "nmoe_decoder_step",
 )
@@ -164,6 +164,8 @@ def lib() -> C.CDLL:
     L.nmoe_full_attn_step.restype = i
     L.nmoe_full_attn_step.argtypes = [C.POINTER(FullAttnWeights), vp, vp, vp, vp, vp, i, i, vp, vp, vp]
     L.nmoe_full_attn_workspace_bytes.restype = sz
+    L.nmoe_linear_attn_step_batched.restype = i
+    L.nmoe_linear_attn_step_batched.argtypes = [C.POINTER(LinearAttnWeights), i, vp, vp, vp, vp, vp, vp, vp, vp]
     L.nmoe_full_attn_step_batched.restype = i
     L.nmoe_full_attn_step_batched.argtypes = [C.POINTER(FullAttnWeights), i, vp, vp, vp, vp, vp, vp, i, vp, vp, vp]
     L.nmoe_full_attn_batched_workspace_bytes.restype = sz
@@ -492,6 +494,17 @@ def linear_attn_step(weights: dict, qkv, z, alpha, beta, conv_state, delta_state
                                      _ptr(delta_state), _ptr(out), stream)
     if rc != OK:
         raise NmoeError(rc, "nmoe_linear_attn_step")
+
+
+def linear_attn_step_batched(weights: dict, qkv, z, alpha, beta, conv_state, delta_state, out, stream=0):
+    """nmoe_linear_attn_step_batched: the step for a batch of sequences (leading dimension
+    of every tensor = the batch)."""
+    w = LinearAttnWeights(_ptr(weights["conv_w"]), _ptr(weights["A_log"]), _ptr(weights["dt_bias"]),
+                          _ptr(weights["norm_w"]))
+    rc = lib().nmoe_linear_attn_step_batched(C.byref(w), int(qkv.shape[0]), _ptr(qkv), _ptr(z), _ptr(alpha),
+                                             _ptr(beta), _ptr(conv_state), _ptr(delta_state), _ptr(out), stream)
+    if rc != OK:
+        raise NmoeError(rc, "nmoe_linear_attn_step_batched")
 
 
 def full_attn_workspace_bytes() -> int:
