@@ -170,14 +170,14 @@ extern "C" nmoe_moe_ctx *nmoe_moe_create(const nmoe_moe_config *cfg, int device,
     ctx->dense_set.assign(cfg->num_layers, 0);
     int bst = nmoe_fused_init(ctx);
     if (bst != NMOE_OK) {
-        snprintf(g_create_error, sizeof g_create_error, "decode kernel init: %s", ctx->last_error);
+        snprintf(g_create_error, sizeof g_create_error, "decode kernel init: %.400s", ctx->last_error);
         *st = bst;
         nmoe_moe_destroy(ctx);
         return nullptr;
     }
     bst = nmoe_batched_init(ctx);
     if (bst != NMOE_OK) {
-        snprintf(g_create_error, sizeof g_create_error, "batched init: %s", ctx->last_error);
+        snprintf(g_create_error, sizeof g_create_error, "batched init: %.400s", ctx->last_error);
         *st = bst;
         nmoe_moe_destroy(ctx);
         return nullptr;
